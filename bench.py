@@ -1,0 +1,602 @@
+"""Decode-attention benchmark (B200): KV-read GB/s and tokens/s.
+
+Workload (default `gqa70b`): the attention of one decode token for every layer of a
+Llama-2-70B-shaped model — 80 layers, 64 query heads, 8 kv heads (GQA group 8),
+head_dim 128, fp16 — for a batch of 32 sequences with 4096 cached keys each
+(+1 appended per step), RoPE theta 1e4 on the new q/k. One step = for each layer,
+one fused launch: RoPE(q, k_new) at T, append (k, v) at T, split-KV attention over
+T+1 keys; the last layer's launch advances seq_len. Steps are replayed from one
+CUDA graph; each step starts by restoring seq_len to 4096 (a 128-byte copy), so
+every timed step has the configured shape. Synthetic data: K/V/q ~ N(0,1) fp16
+from a seed; 43 GB of arena > the 126 MB L2, so no flush is needed between steps.
+
+With --gpus N (one process per GPU under torchrun) the kv heads are sharded:
+each rank owns 8/N kv heads and their 8 query heads each, for all 32 sequences
+("strong" scaling: the whole job is fixed). `--gather-ctx` adds the NCCL
+all-gather of ctx per layer that an unsharded output projection would need.
+
+Other workloads: `gqa70b_32k` (batch 4 at 32768 keys), `varlen7b` (64 sequences,
+lengths U[128, 8192], 32 heads, packed arena with cu_seqlens), `mha7b` (32 heads,
+one sequence at 512 cached keys) — each with --layers.
+
+`--impl reference` times the reference's own implementation of the path: its
+attn_varlen CUDA kernel (built from the reference sources into oracle/_ref)
+driven the way its decode driver drives it (torch RoPE and append per sequence,
+contiguous slice + repeat_interleave, forward), on one layer of the workload
+(a bounded sample), plus the torch-eager fp32 CPU oracle on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "decode-attn KV-read GB/s (% of HBM peak); tokens/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------- workloads
+
+def workload(name: str, layers: int | None):
+    if name == "gqa70b":
+        w = dict(B=32, Hq=64, Hkv=8, D=128, lens=[4096] * 32, layers=80, packed=False)
+    elif name == "gqa70b_32k":
+        w = dict(B=4, Hq=64, Hkv=8, D=128, lens=[32768] * 4, layers=80, packed=False)
+    elif name == "varlen7b":
+        g = torch.Generator().manual_seed(3)
+        lens = torch.randint(128, 8193, (64,), generator=g).tolist()
+        w = dict(B=64, Hq=32, Hkv=32, D=128, lens=lens, layers=32, packed=True)
+    elif name == "mha7b":
+        w = dict(B=1, Hq=32, Hkv=32, D=128, lens=[512], layers=32, packed=False)
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    if layers is not None:
+        w["layers"] = layers
+    w["name"] = name
+    return w
+
+
+def algorithmic_bytes(B, Hq, Hkv, D, lens_plus1, append=True):
+    """Bytes one launch must move: K+V of the attended keys, q in, ctx out, new rows in and out."""
+    kv = sum(lens_plus1) * Hkv * D * 2 * 2
+    qo = B * Hq * D * 2 * 2
+    new = (B * Hkv * D * 2 * 2 * 2) if append else 0
+    return kv + qo + new
+
+
+def kv_read_bytes(Hkv, D, lens_plus1):
+    return sum(lens_plus1) * Hkv * D * 2 * 2
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        if not getattr(self, "out", ""):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(workload_name: str):
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"decode_attn_{workload_name}.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------- distributed
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- our arm
+
+def build_state(w, world, rank, seed=1234):
+    import fully_custom_cuda_inference_lamma2_b200 as fcci
+    from fully_custom_cuda_inference_lamma2_b200.sharding import partition_kv_heads, partition_sequences
+
+    B, Hq, Hkv, D, L = w["B"], w["Hq"], w["Hkv"], w["D"], w["layers"]
+    if w["packed"]:
+        # sequences sharded across ranks
+        seqs = partition_sequences(w["lens"], world)[rank]
+        lens = [w["lens"][i] for i in seqs]
+        hkv, hq = Hkv, Hq
+        caps = [t + 1 for t in lens]
+        arena = fcci.KVArena(L, len(lens), hkv, D, seq_capacities=caps, q_heads=hq)
+    else:
+        kv_lo, kv_hi, q_lo, q_hi = partition_kv_heads(Hkv, Hq, world, rank)
+        hkv, hq = kv_hi - kv_lo, q_hi - q_lo
+        lens = list(w["lens"])
+        arena = fcci.KVArena(L, B, hkv, D, capacity=max(lens) + 1, q_heads=hq)
+    b = len(lens)
+    g = torch.Generator(device="cuda").manual_seed(seed + rank)
+    for t in (arena.k, arena.v):
+        flat = t.view(-1)
+        chunk = 1 << 28
+        for i in range(0, flat.numel(), chunk):
+            flat[i:i + chunk].normal_(generator=g)
+    lens_dev = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    arena.seq_lens.copy_(lens_dev)
+    q = torch.randn(L, b, hq, D, generator=g, device="cuda").half()
+    kn = torch.randn(L, b, hkv, D, generator=g, device="cuda").half()
+    vn = torch.randn(L, b, hkv, D, generator=g, device="cuda").half()
+    out = torch.empty(L, b, hq, D, dtype=torch.float16, device="cuda")
+    return dict(fcci=fcci, arena=arena, lens=lens, lens_dev=lens_dev, q=q, kn=kn, vn=vn, out=out, hq=hq, hkv=hkv,
+                b=b)
+
+
+def run_step(st, gather=None):
+    arena = st["arena"]
+    arena.seq_lens.copy_(st["lens_dev"])
+    L = arena.layers
+    for l in range(L):
+        st["fcci"].decode_attention(arena, l, st["q"][l], st["out"][l], k_new=st["kn"][l], v_new=st["vn"][l],
+                                    advance=(l == L - 1))
+        if gather is not None:
+            gather(l)
+
+
+def ours(args):
+    world, rank, local = dist_setup(args.gpus)
+    w = workload(args.workload, args.layers)
+    st = build_state(w, world, rank)
+    L, D = w["layers"], w["D"]
+    gather = None
+    if args.gather_ctx and world > 1:
+        from fully_custom_cuda_inference_lamma2_b200.sharding import gather_ctx
+
+        full = torch.empty(L, st["b"], w["Hq"], D, dtype=torch.float16, device="cuda")
+
+        def gather(l):
+            gather_ctx(st["out"][l], out=full[l])
+
+    # eager warm-up (sets kernel attributes, NCCL communicators)
+    for _ in range(2):
+        run_step(st, gather)
+    torch.cuda.synchronize()
+    barrier(world)
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(graph, stream=cs):
+            run_step(st, gather)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    lens1 = [t + 1 for t in st["lens"]]
+    per_launch_alg = algorithmic_bytes(st["b"], st["hq"], st["hkv"], D, lens1)
+    per_step_kv = kv_read_bytes(st["hkv"], D, lens1) * L
+    # ---- timed region: K graph replays
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(ms_local, world)
+    ms_step = ms / args.steps
+    kv_all = per_step_kv * args.steps
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([float(kv_all)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        kv_all = float(t.item())
+    value = kv_all / (ms / 1e3) / 1e9
+    tokens_per_s = w["B"] * args.steps / (ms / 1e3)
+    kernel_ms = ms_local / (args.steps * L)  # graph holds only the decode launches (+ one 128 B copy)
+    achieved = per_launch_alg / (kernel_ms / 1e3) / 1e9
+    hbm, hbm_src = peaks()
+    clocks = clk.summary()
+
+    # ---- e2e through the public API with host buffers (pinned), copies overlapped per layer
+    e2e = e2e_run(st, args, L)
+    e2e_ms = max_over_ranks(e2e["ms"], world)
+    e2e_kv = per_step_kv * e2e["steps"]
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([float(e2e_kv)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        e2e_kv = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w, budget_s=args.cpu_seconds)
+
+    del graph
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    traffic = profile_traffic(w["name"])
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) fp16 K/V/q; random-init, no checkpoint)",
+        "config": {
+            "workload": w["name"], "batch": w["B"], "q_heads": w["Hq"], "kv_heads": w["Hkv"], "head_dim": D,
+            "kv_len": (w["lens"][0] if len(set(w["lens"])) == 1 else "seeded U[128,8192]"), "layers": L,
+            "parallelism": ("kv-head shards x%d" % world) if not w["packed"] else ("sequence shards x%d" % world),
+            "gather_ctx": bool(args.gather_ctx and world > 1),
+            "l2": "no flush: arena %.1f GB per GPU > 126 MB L2" % (st["arena"].k.numel() * 4 / 1e9),
+        },
+        "tokens_per_s": round(tokens_per_s, 1),
+        "hbm_frac": round(value / world / hbm, 4),
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved / hbm, 4), "peak_source": hbm_src,
+            "traffic": traffic,
+            "kernel": "decode_attn_kernel<128,1>", "algorithmic_bytes_per_launch": per_launch_alg,
+            "avg_launch_ms": round(kernel_ms, 5),
+        },
+        "e2e": {"value": round(e2e_kv / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                "ms_per_step": round(e2e_ms / e2e["steps"], 4), "api": "attn_varlen.decode per layer, eager",
+                "tokens_per_s": round(w["B"] * e2e["steps"] / (e2e_ms / 1e3), 1)},
+        "gpu_launches": args.steps * L,
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def e2e_run(st, args, L):
+    """Per step: pinned-host q/k_new/v_new -> device (copy stream, one layer ahead),
+    decode through attn_varlen.decode, ctx -> pinned host; timed with events."""
+    arena = st["arena"]
+    hq = st["q"].cpu().pin_memory()
+    hkn = st["kn"].cpu().pin_memory()
+    hvn = st["vn"].cpu().pin_memory()
+    hout = torch.empty(st["out"].shape, dtype=torch.float16).pin_memory()
+    dq, dkn, dvn, dout = st["q"], st["kn"], st["vn"], st["out"]
+    comp = torch.cuda.current_stream()
+    copy_in = torch.cuda.Stream()
+    copy_out = torch.cuda.Stream()
+    steps = max(3, min(args.steps, 10))
+    h2d = (hq.numel() + hkn.numel() + hvn.numel()) * 2
+    d2h = hout.numel() * 2
+
+    def one_step():
+        arena.seq_lens.copy_(st["lens_dev"])
+        ready = [torch.cuda.Event() for _ in range(L)]
+        done = [torch.cuda.Event() for _ in range(L)]
+        copy_in.wait_stream(comp)
+        for l in range(L):
+            with torch.cuda.stream(copy_in):
+                dq[l].copy_(hq[l], non_blocking=True)
+                dkn[l].copy_(hkn[l], non_blocking=True)
+                dvn[l].copy_(hvn[l], non_blocking=True)
+                ready[l].record(copy_in)
+        for l in range(L):
+            comp.wait_event(ready[l])
+            st["fcci"].decode_attention(arena, l, dq[l], dout[l], k_new=dkn[l], v_new=dvn[l], advance=(l == L - 1))
+            done[l].record(comp)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(done[l])
+                hout[l].copy_(dout[l], non_blocking=True)
+        comp.wait_stream(copy_out)
+
+    for _ in range(2):
+        one_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    for _ in range(steps):
+        one_step()
+    e1.record(comp)
+    torch.cuda.synchronize()
+    return {"ms": e0.elapsed_time(e1), "steps": steps, "h2d": h2d, "d2h": d2h}
+
+
+# ---------------------------------------------------------------- CPU oracle baseline
+
+def cpu_threads():
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    return torch.get_num_threads()
+
+
+def cpu_baseline(w, budget_s=10.0, seed=7):
+    """The torch-eager fp32 oracle on the host cores over a bounded sample: one layer's
+    decode step for as many sequences as fit the time budget (whole steps)."""
+    sys.path.insert(0, ROOT)
+    from oracle import decode_oracle as O
+
+    threads = cpu_threads()
+    B, Hq, Hkv, D = w["B"], w["Hq"], w["Hkv"], w["D"]
+    nseq = min(B, 4)
+    lens = w["lens"][:nseq]
+    g = torch.Generator().manual_seed(seed)
+    cap = max(lens) + 1
+    kc = torch.randn(nseq, Hkv, cap, D, generator=g).half()
+    vc = torch.randn(nseq, Hkv, cap, D, generator=g).half()
+    q = torch.randn(nseq, Hq, D, generator=g).half()
+    kn = torch.randn(nseq, Hkv, D, generator=g).half()
+    vn = torch.randn(nseq, Hkv, D, generator=g).half()
+    T = torch.tensor(lens, dtype=torch.int32)
+    O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn, inplace=True)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn, inplace=True)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    kv = kv_read_bytes(Hkv, D, [t + 1 for t in lens]) * n
+    return {"value": round(kv / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"oracle decode_step (torch fp32 eager) on {nseq} of {B} sequences x 1 layer, "
+                      f"{n} repetitions in {dt:.1f} s",
+            "tokens_per_s": round(nseq * n / dt, 2)}
+
+
+# ---------------------------------------------------------------- reference arm
+
+def reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, ROOT)
+    w = workload(args.workload, args.layers)
+    try:
+        import refkernels
+
+        refkernels.ref_attn_varlen()
+    except (OSError, FileNotFoundError) as exc:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference kernel not built: {exc}"}), flush=True)
+        return
+    from oracle import decode_oracle as O  # noqa: F401  (CPU leg below)
+
+    B, Hq, Hkv, D = w["B"], w["Hq"], w["Hkv"], w["D"]
+    G = Hq // Hkv
+    lens = w["lens"]
+    dev = "cuda"
+    gen = torch.Generator(device=dev).manual_seed(99)
+    cap = max(lens) + 1
+    # one layer of the workload: the reference driver's per-sequence steps
+    if w["packed"]:
+        arena_k = [torch.randn(Hkv, t + 1, D, generator=gen, device=dev).half() for t in lens]
+        arena_v = [torch.randn(Hkv, t + 1, D, generator=gen, device=dev).half() for t in lens]
+    else:
+        arena_k = [torch.randn(Hkv, cap, D, generator=gen, device=dev).half() for _ in range(B)]
+        arena_v = [torch.randn(Hkv, cap, D, generator=gen, device=dev).half() for _ in range(B)]
+    q = torch.randn(B, Hq, D, generator=gen, device=dev).half()
+    kn = torch.randn(B, Hkv, D, generator=gen, device=dev).half()
+    vn = torch.randn(B, Hkv, D, generator=gen, device=dev).half()
+    scale = 1.0 / math.sqrt(D)
+    inv = (10000.0 ** (-torch.arange(D // 2, device=dev, dtype=torch.float32) / float(D // 2))).view(1, -1)
+
+    def rope_(hd, pos):  # the driver's apply_rope_ math, on the device as it runs it
+        half = D // 2
+        ang = pos * inv
+        c, s = torch.cos(ang), torch.sin(ang)
+        x1, x2 = hd[:, :half].float(), hd[:, half:].float()
+        r1, r2 = (x1 * c - x2 * s).to(hd.dtype), (x2 * c + x1 * s).to(hd.dtype)
+        hd[:, :half] = r1
+        hd[:, half:] = r2
+        return hd
+
+    def layer_step(kernel_only_ms=None):
+        for b in range(B):
+            T = lens[b]
+            qh = rope_(q[b].clone(), T)
+            kh = rope_(kn[b].clone(), T)
+            arena_k[b][:, T].copy_(kh)
+            arena_v[b][:, T].copy_(vn[b])
+            Ks = arena_k[b][:, :T + 1].contiguous().repeat_interleave(G, dim=0)
+            Vs = arena_v[b][:, :T + 1].contiguous().repeat_interleave(G, dim=0)
+            refkernels.ref_forward(qh, Ks, Vs, T + 1, scale)
+
+    layer_step()
+    torch.cuda.synchronize()
+    steps = max(1, args.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.warmup):
+        layer_step()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        layer_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    lens1 = [t + 1 for t in lens]
+    kv = kv_read_bytes(Hkv, D, lens1) * steps
+    value = kv / (ms / 1e3) / 1e9
+    # kernel alone on pre-built inputs (first sequence), for context
+    T = lens[0]
+    Ks = arena_k[0][:, :T + 1].contiguous().repeat_interleave(G, dim=0)
+    Vs = arena_v[0][:, :T + 1].contiguous().repeat_interleave(G, dim=0)
+    qh = q[0].clone()
+    refkernels.ref_forward(qh, Ks, Vs, T + 1, scale)
+    torch.cuda.synchronize()
+    e0.record()
+    reps = 5
+    for _ in range(reps):
+        refkernels.ref_forward(qh, Ks, Vs, T + 1, scale)
+    e1.record()
+    torch.cuda.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    k_gbs = kv_read_bytes(Hkv, D, [T + 1]) / (k_ms / 1e3) / 1e9
+    cpu = cpu_baseline(w, budget_s=args.cpu_seconds) if not args.no_cpu_baseline else None
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / steps, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) fp16)",
+        "config": {"workload": w["name"], "batch": B, "q_heads": Hq, "kv_heads": Hkv, "head_dim": D,
+                   "layers_timed_per_step": 1, "layers": w["layers"],
+                   "sample": "one layer of the workload per step (bounded sample)"},
+        "tokens_per_s_per_layer": round(B * steps / (ms / 1e3), 2),
+        "implementation": ("reference custom_kernels/attn_varlen_kernel.cu built from source for sm_100a "
+                           "(oracle/_ref), driven as scripts/direct_custom_decode_500.py:229-250 does: "
+                           "torch RoPE, append, contiguous slice, repeat_interleave, attn_varlen forward"),
+        "kernel_only": {"value": round(k_gbs, 2), "unit": "GB/s", "ms_per_sequence": round(k_ms, 3)},
+        "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if world > 1:
+        line["note"] = f"rank 0 of {world} ran the single-GPU reference; other ranks idle"
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="gqa70b", choices=["gqa70b", "gqa70b_32k", "varlen7b", "mha7b"])
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--gather-ctx", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        reference(args)
+    else:
+        ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,1004 @@
+// Varlen split-KV decode attention for B200 (sm_100a), with RoPE, KV append and
+// device-side seq_len bookkeeping fused into the same launch.
+//
+// Replaces, for one decode token per sequence:
+//   - custom_kernels/attn_varlen_kernel.cu:9-86 (attention of one query per head)
+//   - the torch RoPE / append / gather / repeat_interleave steps of the decode
+//     drivers (scripts/direct_custom_decode_500.py:229-250)
+//   - the seq_len bump of capture_decode_step_kernel.cu:95-99
+//
+// Work decomposition. A "pair" is (sequence b, kv head h); its L_b keys are cut
+// into tiles of 64 keys. All tiles of all pairs form one line of N tiles. In
+// split mode a persistent grid of C CTAs takes contiguous ranges
+// [c*N/C, (c+1)*N/C) (stream-K), so every CTA streams the same number of tiles
+// whatever the length mix. A pair lying inside one CTA's range is finished by
+// that CTA; a pair cut by CTA boundaries leaves one partial (o, lse) per piece
+// in slot (pair + cta) — unique because both cut sets are ordered — and the
+// last piece to finish (atomic counter, never waited on) merges them. In pair
+// mode there is one CTA per pair and no workspace.
+//
+// Inside a CTA: warp 4 is the TMA producer (one thread), warps 0..3 consume.
+// A stage holds the K and V tiles of 64 keys (2 x 64 x D fp16), loaded as
+// 16-row x 64-col boxes with 128-byte swizzle through a 4-D tensor map
+// (head_dim, token, kv head, sequence); only boxes holding valid keys are
+// fetched. Consumer warp w owns keys [16w, 16w+16) of each tile:
+//   S^T[key, head] = K Q^T     (mma m16n8k16: A = K rows via ldmatrix, B = the
+//                               rotated queries of the GQA group, n = 8 heads)
+//   online softmax per head column (quad shuffles), P^T -> B fragments with
+//   movmatrix.trans,
+//   O^T[dim, head] += V^T P^T  (A = V via ldmatrix.trans)
+// so a group of 8 query heads fills the n=8 MMA tile exactly and every K/V byte
+// is read from HBM once per group.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "fcci_decode.h"
+#include "fcci_internal.h"
+#include "ptx.cuh"
+
+namespace fcci {
+
+constexpr int kTileKeys = 64;
+constexpr int kGroupKeys = 16;
+constexpr int kConsumerWarps = 4;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kBoxBytes = kGroupKeys * 128;  // 16 rows x 64 fp16
+constexpr int kHalfTileBytes = kTileKeys * 128;
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any healthy wait
+constexpr uint64_t kDrainLimitNs = 500000000ull;
+constexpr int kConsumerBar = 1;
+
+struct Params {
+    const __half* q;
+    int64_t q_sb, q_sh;
+    const __half* k_new;
+    int64_t kn_sb, kn_sh;
+    const __half* v_new;
+    int64_t vn_sb, vn_sh;
+    __half* k_cache;
+    int64_t k_sb, k_sh, k_st;
+    __half* v_cache;
+    int64_t v_sb, v_sh, v_st;
+    int32_t capacity;
+    const int32_t* cu_seqlens;
+    int32_t* seq_lens;
+    int32_t fixed_len;
+    __half* out;
+    int64_t o_sb, o_sh;
+    __half* q_rot_out;
+    float scale_log2;
+    float rope_theta;
+    int32_t rotary_dim;
+    int32_t advance;
+    int32_t append;
+    int32_t split;
+    int32_t B, Hq, Hkv, G;
+    int32_t stages;
+    uint32_t* err;
+    uint32_t* done_cnt;
+    uint32_t* pair_cnt;
+    float* part_lse;
+    float* part_o;
+};
+
+struct SeqInfo {
+    int T;         // cached length before this step
+    int L;         // keys attended (0 when the sequence is invalid)
+    int tok_base;  // first token row of the sequence in the arena
+    bool ok;
+};
+
+__device__ __forceinline__ SeqInfo seq_info(const Params& p, int b) {
+    SeqInfo s;
+    s.T = p.seq_lens ? p.seq_lens[b] : p.fixed_len;
+    int cap = p.capacity;
+    s.tok_base = 0;
+    bool ok = true;
+    if (p.cu_seqlens) {
+        const int lo = p.cu_seqlens[b], hi = p.cu_seqlens[b + 1];
+        s.tok_base = lo;
+        cap = hi - lo;
+        ok = lo >= 0 && hi >= lo && hi <= p.capacity;
+    }
+    s.L = s.T + p.append;
+    ok = ok && s.T >= 0 && s.L <= cap;
+    s.ok = ok;
+    if (!ok) s.L = 0;
+    return s;
+}
+
+__device__ __forceinline__ int tiles_of(int L) { return L > 0 ? (L + kTileKeys - 1) / kTileKeys : 1; }
+
+__device__ __forceinline__ void set_error(const Params& p, uint32_t bit) {
+    if (p.err) atomicOr(p.err, bit);
+}
+
+// ceil((t+1)*C/N) - 1: the CTA whose range [c*N/C, (c+1)*N/C) contains tile t.
+__device__ __forceinline__ int cta_of_tile(long long t, long long N, long long C) {
+    return (int)(((t + 1) * C + N - 1) / N - 1);
+}
+
+// Accurate RoPE table entry i for position pos: the reference computes
+// inv = theta ** (-i / half) and angle = pos * inv in fp32, then cos/sin in fp32
+// (scripts/direct_custom_decode_500.py:96-100).
+__device__ __forceinline__ float2 rope_cs_entry(float theta, int i, int half, int pos) {
+    const float e = __fdiv_rn(-(float)i, (float)half);
+    const float inv = powf(theta, e);
+    const float ang = __fmul_rn((float)pos, inv);
+    return make_float2(cosf(ang), sinf(ang));
+}
+
+// One rotate-half element, rounded exactly as the reference's separate torch ops:
+// x1' = x1*cos - x2*sin, x2' = x2*cos + x1*sin (direct_custom_decode_500.py:103-104).
+__device__ __forceinline__ float rope_elem(float x, float partner, float2 cs, bool first_half) {
+    return first_half ? __fsub_rn(__fmul_rn(x, cs.x), __fmul_rn(partner, cs.y))
+                      : __fadd_rn(__fmul_rn(x, cs.x), __fmul_rn(partner, cs.y));
+}
+
+template <int D, int NB>
+struct Layout {
+    static constexpr int G8 = 8 * NB;
+    static constexpr int KT = 128 * D;  // bytes of one 64-key tile of K (or V)
+    static constexpr int RP = D + 4;    // fp32 pitch of the cross-warp reduction rows
+    static constexpr int QP = D + 8;    // fp16 pitch of the rotated-query rows
+    static __host__ __device__ constexpr size_t stage_bytes() { return 2 * (size_t)KT; }
+    static __host__ __device__ constexpr size_t fixed_bytes(int stages) {
+        return (size_t)stages * stage_bytes() + sizeof(float) * kConsumerWarps * G8 * RP +
+               sizeof(float) * kConsumerWarps * G8 * 2 + sizeof(__half) * G8 * QP + sizeof(float2) * (D / 2) +
+               sizeof(uint64_t) * 2 * stages + sizeof(int) * 8;
+    }
+    static __host__ size_t smem_bytes(int stages, int B, bool split) {
+        return 1024 + fixed_bytes(stages) + (split ? sizeof(int) * (B + 1) : 0);
+    }
+};
+
+template <int D, int NB>
+__global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                               const __grid_constant__ CUtensorMap tmV,
+                                                               const Params p) {
+    using LY = Layout<D, NB>;
+    constexpr int G8 = LY::G8;
+    constexpr int KT = LY::KT;
+    constexpr int RP = LY::RP;
+    constexpr int QP = LY::QP;
+    constexpr int HALVES = D / 64;
+    constexpr int KSTEPS = D / 16;
+    constexpr int E = D / 32;  // elements of a row per lane
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = p.stages;
+    uint8_t* stages = sm;
+    float* red_acc = reinterpret_cast<float*>(stages + (size_t)S * LY::stage_bytes());
+    float* red_ml = red_acc + kConsumerWarps * G8 * RP;
+    __half* qrot = reinterpret_cast<__half*>(red_ml + kConsumerWarps * G8 * 2);
+    float2* rope_cs = reinterpret_cast<float2*>(qrot + G8 * QP);
+    uint64_t* full = reinterpret_cast<uint64_t*>(rope_cs + D / 2);
+    uint64_t* empty = full + S;
+    int* misc = reinterpret_cast<int*>(empty + S);
+    int* tile_base = misc + 8;
+    volatile int* abort_flag = misc;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int B = p.B, Hkv = p.Hkv, G = p.G;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        misc[0] = 0;
+        misc[1] = 0;
+        fence_mbar_init();
+    }
+    if (tid == kConsumerThreads) {
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+    }
+
+    // ---- tile line: per-sequence tile counts and their prefix (split mode)
+    if (p.split) {
+        int* scratch = reinterpret_cast<int*>(red_acc);  // free until the first segment ends
+        const int chunk = (B + kThreads - 1) / kThreads;
+        const int lo = tid * chunk, hi = min(B, lo + chunk);
+        int local = 0;
+        for (int b = lo; b < hi; ++b) {
+            const SeqInfo si = seq_info(p, b);
+            if (!si.ok && blockIdx.x == 0) set_error(p, FCCI_DEV_ERR_CAPACITY);
+            const int c = tiles_of(si.L) * Hkv;
+            tile_base[b + 1] = c;
+            local += c;
+        }
+        scratch[tid] = local;
+        __syncthreads();
+        if (tid == 0) {
+            int run = 0;
+            for (int i = 0; i < kThreads; ++i) {
+                const int v = scratch[i];
+                scratch[i] = run;
+                run += v;
+            }
+            tile_base[0] = 0;
+        }
+        __syncthreads();
+        int run = scratch[tid];
+        for (int b = lo; b < hi; ++b) {
+            run += tile_base[b + 1];
+            tile_base[b + 1] = run;
+        }
+    } else if (tid == 0 && p.err) {
+        const SeqInfo si = seq_info(p, blockIdx.x / Hkv);
+        if (!si.ok && (blockIdx.x % Hkv) == 0) set_error(p, FCCI_DEV_ERR_CAPACITY);
+    }
+    __syncthreads();
+
+    // ---- this CTA's tile range
+    long long t_begin = 0, t_end = 0, N = 0;
+    int b0 = 0, h0 = 0, j0 = 0;
+    if (p.split) {
+        N = tile_base[B];
+        t_begin = (long long)blockIdx.x * N / gridDim.x;
+        t_end = ((long long)blockIdx.x + 1) * N / gridDim.x;
+        if (t_begin < t_end) {
+            int lo = 0, hi = B - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (tile_base[mid] <= t_begin) lo = mid;
+                else hi = mid - 1;
+            }
+            b0 = lo;
+            const int tiles = (tile_base[b0 + 1] - tile_base[b0]) / Hkv;
+            const int rem = (int)(t_begin - tile_base[b0]);
+            h0 = rem / tiles;
+            j0 = rem - h0 * tiles;
+        }
+    } else {
+        b0 = blockIdx.x / Hkv;
+        h0 = blockIdx.x - b0 * Hkv;
+        j0 = 0;
+        t_begin = 0;
+        t_end = tiles_of(seq_info(p, b0).L);
+    }
+    const int ntiles = (int)(t_end - t_begin);
+
+    if (warp == kConsumerWarps) {
+        // ============================================================ producer
+        if (lane == 0 && ntiles > 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int b = b0, h = h0, j = j0;
+            SeqInfo si = seq_info(p, b);
+            int tiles = tiles_of(si.L);
+            int issued = 0;
+            for (int it = 0; it < ntiles; ++it) {
+                const int s = it % S;
+                const uint32_t ph = (uint32_t)(it / S) & 1u;
+                if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag, kWaitLimitNs)) {
+                    *abort_flag = 1;
+                    set_error(p, FCCI_DEV_ERR_TIMEOUT);
+                    break;
+                }
+                const int nv = min(kTileKeys, si.L - kTileKeys * j);
+                const int ngr = nv > 0 ? (nv + kGroupKeys - 1) / kGroupKeys : 0;
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(ngr * 64 * D));
+                uint8_t* kdst = stages + (size_t)s * LY::stage_bytes();
+                uint8_t* vdst = kdst + KT;
+                const int row0 = si.tok_base + kTileKeys * j;
+                const int c3 = p.cu_seqlens ? 0 : b;
+                for (int g = 0; g < ngr; ++g) {
+#pragma unroll
+                    for (int hf = 0; hf < HALVES; ++hf) {
+                        tma_load_4d(kdst + hf * kHalfTileBytes + g * kBoxBytes, &tmK, hf * 64, row0 + kGroupKeys * g, h,
+                                    c3, &full[s], pol);
+                        tma_load_4d(vdst + hf * kHalfTileBytes + g * kBoxBytes, &tmV, hf * 64, row0 + kGroupKeys * g, h,
+                                    c3, &full[s], pol);
+                    }
+                }
+                ++issued;
+                if (++j == tiles) {
+                    j = 0;
+                    if (++h == Hkv) {
+                        h = 0;
+                        if (++b < B) {
+                            si = seq_info(p, b);
+                            tiles = tiles_of(si.L);
+                        }
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // let copies still in flight land before the CTA can exit
+                for (int it = max(0, issued - S); it < issued; ++it) {
+                    volatile int never = 0;
+                    mbar_wait_bounded(&full[it % S], (uint32_t)(it / S) & 1u, &never, kDrainLimitNs);
+                }
+            }
+        }
+    } else {
+        // ============================================================ consumers
+        const int w = warp;
+        const int ctid = tid;  // 0..127
+        const int g = lane >> 2, t4 = lane & 3;
+        const int mi = lane >> 3;
+        const uint32_t swz = (uint32_t)(lane & 7);
+        const int rot = p.rotary_dim;
+        const int rhalf = rot >> 1;
+
+        float m[NB][2], l[NB][2], acc[NB][KSTEPS][4];
+        uint32_t qf[NB][KSTEPS][2];
+        int cached_pos = -1;
+
+        int b = b0, h = h0, j = j0;
+        SeqInfo si = seq_info(p, b);
+        int tiles = tiles_of(si.L);
+        bool seg_start = true;
+
+        for (int it = 0; it < ntiles; ++it) {
+            if (seg_start) {
+                seg_start = false;
+                // ---- rotated queries of the group (shared by the 4 warps)
+                if (rot > 0 && si.T != cached_pos) {
+                    for (int i = ctid; i < rhalf; i += kConsumerThreads)
+                        rope_cs[i] = rope_cs_entry(p.rope_theta, i, rhalf, si.T);
+                    cached_pos = si.T;
+                    named_bar_sync(kConsumerBar, kConsumerThreads);
+                }
+                const bool write_qrot = (p.q_rot_out != nullptr) && (j == 0);
+                const __half* qb = p.q + (int64_t)b * p.q_sb;
+                for (int e = ctid; e < G8 * D; e += kConsumerThreads) {
+                    const int hh = e / D;
+                    const int d = e - hh * D;
+                    __half val = __float2half_rn(0.f);
+                    if (hh < G) {
+                        const __half* qr = qb + (int64_t)(h * G + hh) * p.q_sh;
+                        if (d < rot) {
+                            const bool first = d < rhalf;
+                            const int i = first ? d : d - rhalf;
+                            const float x = __half2float(qr[d]);
+                            const float xp = __half2float(qr[first ? d + rhalf : d - rhalf]);
+                            val = __float2half_rn(rope_elem(x, xp, rope_cs[i], first));
+                        } else {
+                            val = qr[d];
+                        }
+                        if (write_qrot) p.q_rot_out[((int64_t)b * p.Hq + h * G + hh) * D + d] = val;
+                    }
+                    qrot[hh * QP + d] = val;
+                }
+                named_bar_sync(kConsumerBar, kConsumerThreads);
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+                    for (int kk = 0; kk < KSTEPS; ++kk) {
+                        const __half* qrow = qrot + (nb * 8 + g) * QP + 16 * kk + 2 * t4;
+                        qf[nb][kk][0] = *reinterpret_cast<const uint32_t*>(qrow);
+                        qf[nb][kk][1] = *reinterpret_cast<const uint32_t*>(qrow + 8);
+                    }
+                    m[nb][0] = m[nb][1] = -INFINITY;
+                    l[nb][0] = l[nb][1] = 0.f;
+#pragma unroll
+                    for (int mb = 0; mb < KSTEPS; ++mb) acc[nb][mb][0] = acc[nb][mb][1] = acc[nb][mb][2] = acc[nb][mb][3] = 0.f;
+                }
+            }
+
+            const int s = it % S;
+            const bool ready = mbar_wait_bounded(&full[s], (uint32_t)(it / S) & 1u, abort_flag, kWaitLimitNs);
+            if (!ready && !*abort_flag) {
+                *abort_flag = 1;
+                set_error(p, FCCI_DEV_ERR_TIMEOUT);
+            }
+            const int key0 = kTileKeys * j + kGroupKeys * w;
+            const int nvw = max(0, min(kGroupKeys, si.L - key0));
+            if (ready && nvw > 0) {
+                uint8_t* kt = stages + (size_t)s * LY::stage_bytes();
+                uint8_t* vt = kt + KT;
+                const int row_base = kGroupKeys * w;
+                bool wrote = false;
+                // ---- append: rotated k_new and v_new become key T of this pair
+                if (p.append && si.T >= key0 && si.T < key0 + kGroupKeys) {
+                    const int r = si.T - kTileKeys * j;
+                    const int d0 = lane * E;
+                    const __half* kn = p.k_new + (int64_t)b * p.kn_sb + (int64_t)h * p.kn_sh;
+                    const __half* vn = p.v_new + (int64_t)b * p.vn_sb + (int64_t)h * p.vn_sh;
+                    __align__(16) __half kr[E];
+                    __align__(16) __half vr[E];
+#pragma unroll
+                    for (int e = 0; e < E; ++e) {
+                        const int d = d0 + e;
+                        if (d < rot) {
+                            const bool first = d < rhalf;
+                            const int i = first ? d : d - rhalf;
+                            const float x = __half2float(kn[d]);
+                            const float xp = __half2float(kn[first ? d + rhalf : d - rhalf]);
+                            kr[e] = __float2half_rn(rope_elem(x, xp, rope_cs[i], first));
+                        } else {
+                            kr[e] = kn[d];
+                        }
+                        vr[e] = vn[d];
+                    }
+                    const int64_t bofs_k = p.cu_seqlens ? 0 : (int64_t)b * p.k_sb;
+                    const int64_t bofs_v = p.cu_seqlens ? 0 : (int64_t)b * p.v_sb;
+                    __half* kdst = p.k_cache + bofs_k + (int64_t)h * p.k_sh + (int64_t)(si.tok_base + si.T) * p.k_st + d0;
+                    __half* vdst = p.v_cache + bofs_v + (int64_t)h * p.v_sh + (int64_t)(si.tok_base + si.T) * p.v_st + d0;
+                    const uint32_t so = (uint32_t)((d0 >> 6) * kHalfTileBytes + r * 128 +
+                                                   ((((d0 & 63) >> 3) ^ (r & 7)) << 4) + (d0 & 7) * 2);
+                    if constexpr (E == 2) {
+                        *reinterpret_cast<uint32_t*>(kdst) = *reinterpret_cast<uint32_t*>(kr);
+                        *reinterpret_cast<uint32_t*>(vdst) = *reinterpret_cast<uint32_t*>(vr);
+                        *reinterpret_cast<uint32_t*>(kt + so) = *reinterpret_cast<uint32_t*>(kr);
+                        *reinterpret_cast<uint32_t*>(vt + so) = *reinterpret_cast<uint32_t*>(vr);
+                    } else if constexpr (E == 4) {
+                        *reinterpret_cast<uint2*>(kdst) = *reinterpret_cast<uint2*>(kr);
+                        *reinterpret_cast<uint2*>(vdst) = *reinterpret_cast<uint2*>(vr);
+                        *reinterpret_cast<uint2*>(kt + so) = *reinterpret_cast<uint2*>(kr);
+                        *reinterpret_cast<uint2*>(vt + so) = *reinterpret_cast<uint2*>(vr);
+                    } else {
+                        *reinterpret_cast<uint4*>(kdst) = *reinterpret_cast<uint4*>(kr);
+                        *reinterpret_cast<uint4*>(vdst) = *reinterpret_cast<uint4*>(vr);
+                        *reinterpret_cast<uint4*>(kt + so) = *reinterpret_cast<uint4*>(kr);
+                        *reinterpret_cast<uint4*>(vt + so) = *reinterpret_cast<uint4*>(vr);
+                    }
+                    wrote = true;
+                }
+                // ---- keys past the end: zero their V rows so 0 * garbage cannot make NaN
+                if (nvw < kGroupKeys) {
+                    const int nz = kGroupKeys - nvw;
+                    for (int c = lane; c < nz * HALVES * 8; c += 32) {
+                        const int r = row_base + nvw + c / (HALVES * 8);
+                        const int rem = c % (HALVES * 8);
+                        *reinterpret_cast<uint4*>(vt + (rem >> 3) * kHalfTileBytes + r * 128 + (rem & 7) * 16) =
+                            make_uint4(0u, 0u, 0u, 0u);
+                    }
+                    wrote = true;
+                }
+                if (wrote) __syncwarp();
+
+                // ---- S^T = K Q^T over the 16 keys of this warp
+                const uint32_t kbase = smem_u32(kt);
+                const uint32_t vbase = smem_u32(vt);
+                const int rowA = row_base + (lane & 7) + ((mi & 1) << 3);
+                float s0[NB][4], s1[NB][4];
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) s0[nb][c] = s1[nb][c] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < KSTEPS; ++kk) {
+                    const int chunk = 2 * kk + (mi >> 1);
+                    const uint32_t addr =
+                        kbase + (chunk >> 3) * kHalfTileBytes + rowA * 128 + ((((uint32_t)chunk & 7u) ^ swz) << 4);
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(addr, a0, a1, a2, a3);
+#pragma unroll
+                    for (int nb = 0; nb < NB; ++nb) {
+                        if (kk & 1) mma_16816(s1[nb], a0, a1, a2, a3, qf[nb][kk][0], qf[nb][kk][1]);
+                        else mma_16816(s0[nb], a0, a1, a2, a3, qf[nb][kk][0], qf[nb][kk][1]);
+                    }
+                }
+                // ---- online softmax per head column (log2 domain)
+                const bool v0 = g < nvw;
+                const bool v8 = (g + 8) < nvw;
+                uint32_t pb0[NB], pb1[NB];
+                float alpha[NB][2];
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const float x0 = v0 ? (s0[nb][0] + s1[nb][0]) * p.scale_log2 : -INFINITY;
+                    const float x1 = v0 ? (s0[nb][1] + s1[nb][1]) * p.scale_log2 : -INFINITY;
+                    const float x2 = v8 ? (s0[nb][2] + s1[nb][2]) * p.scale_log2 : -INFINITY;
+                    const float x3 = v8 ? (s0[nb][3] + s1[nb][3]) * p.scale_log2 : -INFINITY;
+                    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 4));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 4));
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 8));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 8));
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 16));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 16));
+                    const float mn0 = fmaxf(m[nb][0], mx0);
+                    const float mn1 = fmaxf(m[nb][1], mx1);
+                    alpha[nb][0] = ex2(m[nb][0] - mn0);
+                    alpha[nb][1] = ex2(m[nb][1] - mn1);
+                    const float p0 = ex2(x0 - mn0), p1 = ex2(x1 - mn1);
+                    const float p2 = ex2(x2 - mn0), p3 = ex2(x3 - mn1);
+                    l[nb][0] = l[nb][0] * alpha[nb][0] + (p0 + p2);
+                    l[nb][1] = l[nb][1] * alpha[nb][1] + (p1 + p3);
+                    m[nb][0] = mn0;
+                    m[nb][1] = mn1;
+                    pb0[nb] = movmatrix_t(pack_half2(p0, p1));
+                    pb1[nb] = movmatrix_t(pack_half2(p2, p3));
+                }
+                // ---- O^T += V^T P^T
+                const int rowV = row_base + (lane & 7) + ((mi >> 1) << 3);
+#pragma unroll
+                for (int mb = 0; mb < KSTEPS; ++mb) {
+                    const int chunk = 2 * mb + (mi & 1);
+                    const uint32_t addr =
+                        vbase + (chunk >> 3) * kHalfTileBytes + rowV * 128 + ((((uint32_t)chunk & 7u) ^ swz) << 4);
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(addr, a0, a1, a2, a3);
+#pragma unroll
+                    for (int nb = 0; nb < NB; ++nb) {
+                        acc[nb][mb][0] *= alpha[nb][0];
+                        acc[nb][mb][1] *= alpha[nb][1];
+                        acc[nb][mb][2] *= alpha[nb][0];
+                        acc[nb][mb][3] *= alpha[nb][1];
+                        mma_16816(acc[nb][mb], a0, a1, a2, a3, pb0[nb], pb1[nb]);
+                    }
+                }
+                if (wrote) fence_proxy_async_smem();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+
+            const bool seg_end = (j == tiles - 1) || (it == ntiles - 1);
+            if (seg_end) {
+                // ---- merge the 4 warps' states through shared memory
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    float l0 = l[nb][0], l1 = l[nb][1];
+                    l0 += __shfl_xor_sync(0xffffffffu, l0, 4);
+                    l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
+                    l0 += __shfl_xor_sync(0xffffffffu, l0, 8);
+                    l1 += __shfl_xor_sync(0xffffffffu, l1, 8);
+                    l0 += __shfl_xor_sync(0xffffffffu, l0, 16);
+                    l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
+                    const int hA = nb * 8 + 2 * t4;
+                    if (g == 0) {
+                        red_ml[(w * G8 + hA) * 2 + 0] = m[nb][0];
+                        red_ml[(w * G8 + hA) * 2 + 1] = l0;
+                        red_ml[(w * G8 + hA + 1) * 2 + 0] = m[nb][1];
+                        red_ml[(w * G8 + hA + 1) * 2 + 1] = l1;
+                    }
+                    float* ra = red_acc + (w * G8 + hA) * RP;
+#pragma unroll
+                    for (int mb = 0; mb < KSTEPS; ++mb) {
+                        const int d = 16 * mb + g;
+                        ra[d] = acc[nb][mb][0];
+                        ra[RP + d] = acc[nb][mb][1];
+                        ra[d + 8] = acc[nb][mb][2];
+                        ra[RP + d + 8] = acc[nb][mb][3];
+                    }
+                }
+                named_bar_sync(kConsumerBar, kConsumerThreads);
+
+                const int pidx = b * Hkv + h;
+                bool whole = true;
+                int c0 = 0, c1 = 0;
+                if (p.split) {
+                    const long long pfirst = tile_base[b] + (long long)h * tiles;
+                    c0 = cta_of_tile(pfirst, N, gridDim.x);
+                    c1 = cta_of_tile(pfirst + tiles - 1, N, gridDim.x);
+                    whole = (c0 == c1);
+                }
+                const int slot = pidx + blockIdx.x;
+                __half* ob = p.out + (int64_t)b * p.o_sb;
+                for (int e = ctid * 2; e < G * D; e += 2 * kConsumerThreads) {
+                    const int hh = e / D;
+                    const int d = e - hh * D;
+                    float M = -INFINITY;
+#pragma unroll
+                    for (int ww = 0; ww < kConsumerWarps; ++ww) M = fmaxf(M, red_ml[(ww * G8 + hh) * 2]);
+                    float Ls = 0.f, o0 = 0.f, o1 = 0.f;
+                    if (M != -INFINITY) {
+#pragma unroll
+                        for (int ww = 0; ww < kConsumerWarps; ++ww) {
+                            const float sc = ex2(red_ml[(ww * G8 + hh) * 2] - M);
+                            Ls += red_ml[(ww * G8 + hh) * 2 + 1] * sc;
+                            o0 += red_acc[(ww * G8 + hh) * RP + d] * sc;
+                            o1 += red_acc[(ww * G8 + hh) * RP + d + 1] * sc;
+                        }
+                    }
+                    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+                    if (whole) {
+                        *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) =
+                            __floats2half2_rn(o0 * inv, o1 * inv);
+                    } else {
+                        *reinterpret_cast<float2*>(p.part_o + ((size_t)slot * G + hh) * D + d) =
+                            make_float2(o0 * inv, o1 * inv);
+                        if (d == 0) p.part_lse[(size_t)slot * G + hh] = Ls > 0.f ? M + __log2f(Ls) : -INFINITY;
+                    }
+                }
+                named_bar_sync(kConsumerBar, kConsumerThreads);
+                if (!whole) {
+                    // ---- the last piece of a cut pair merges every piece's (o, lse)
+                    __threadfence();
+                    named_bar_sync(kConsumerBar, kConsumerThreads);
+                    if (ctid == 0) {
+                        const unsigned old = atomicAdd(&p.pair_cnt[pidx], 1u);
+                        misc[1] = (old == (unsigned)(c1 - c0)) ? 1 : 0;
+                    }
+                    named_bar_sync(kConsumerBar, kConsumerThreads);
+                    if (misc[1]) {
+                        __threadfence();
+                        for (int e = ctid * 2; e < G * D; e += 2 * kConsumerThreads) {
+                            const int hh = e / D;
+                            const int d = e - hh * D;
+                            float LSE = -INFINITY;
+                            for (int c = c0; c <= c1; ++c)
+                                LSE = fmaxf(LSE, __ldcg(p.part_lse + (size_t)(pidx + c) * G + hh));
+                            float W = 0.f, o0 = 0.f, o1 = 0.f;
+                            if (LSE != -INFINITY) {
+                                for (int c = c0; c <= c1; ++c) {
+                                    const float wgt = ex2(__ldcg(p.part_lse + (size_t)(pidx + c) * G + hh) - LSE);
+                                    const float2 v =
+                                        __ldcg(reinterpret_cast<const float2*>(p.part_o + ((size_t)(pidx + c) * G + hh) * D + d));
+                                    W += wgt;
+                                    o0 += wgt * v.x;
+                                    o1 += wgt * v.y;
+                                }
+                            }
+                            const float inv = W > 0.f ? 1.f / W : 0.f;
+                            *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) =
+                                __floats2half2_rn(o0 * inv, o1 * inv);
+                        }
+                        if (ctid == 0) atomicExch(&p.pair_cnt[pidx], 0u);
+                    }
+                }
+                seg_start = true;
+            }
+
+            if (++j == tiles) {
+                j = 0;
+                if (++h == Hkv) {
+                    h = 0;
+                    if (++b < B) {
+                        si = seq_info(p, b);
+                        tiles = tiles_of(si.L);
+                    }
+                }
+            }
+        }
+    }
+
+    __syncthreads();
+    // ---- device-side seq_len advance once every CTA has read the lengths
+    if (p.advance) {
+        if (tid == 0) {
+            __threadfence();
+            const unsigned old = atomicAdd(p.done_cnt, 1u);
+            misc[1] = (old == gridDim.x - 1) ? 1 : 0;
+        }
+        __syncthreads();
+        if (misc[1]) {
+            __threadfence();
+            for (int b = tid; b < B; b += kThreads) {
+                const SeqInfo si = seq_info(p, b);
+                if (si.ok) p.seq_lens[b] = si.T + 1;
+            }
+            if (tid == 0) atomicExch(p.done_cnt, 0u);
+        }
+    }
+}
+
+// RoPE(q, k_new) at T_b and append of (k_rot, v_new); one CTA per sequence.
+template <int D>
+__global__ void __launch_bounds__(128) rope_append_kernel(const Params p) {
+    constexpr int E = D / 32;
+    __shared__ float2 cs[D / 2];
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const SeqInfo si = seq_info(p, b);
+    const int rot = p.rotary_dim, rhalf = rot >> 1;
+    if (!si.ok) {
+        if (tid == 0) set_error(p, FCCI_DEV_ERR_CAPACITY);
+        return;
+    }
+    for (int i = tid; i < rhalf; i += blockDim.x) cs[i] = rope_cs_entry(p.rope_theta, i, rhalf, si.T);
+    __syncthreads();
+    for (int h = warp; h < p.Hkv; h += blockDim.x / 32) {
+        const __half* kn = p.k_new + (int64_t)b * p.kn_sb + (int64_t)h * p.kn_sh;
+        const __half* vn = p.v_new + (int64_t)b * p.vn_sb + (int64_t)h * p.vn_sh;
+        const int64_t bofs_k = p.cu_seqlens ? 0 : (int64_t)b * p.k_sb;
+        const int64_t bofs_v = p.cu_seqlens ? 0 : (int64_t)b * p.v_sb;
+        __half* kd = p.k_cache + bofs_k + (int64_t)h * p.k_sh + (int64_t)(si.tok_base + si.T) * p.k_st;
+        __half* vd = p.v_cache + bofs_v + (int64_t)h * p.v_sh + (int64_t)(si.tok_base + si.T) * p.v_st;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const int d = lane * E + e;
+            __half r;
+            if (d < rot) {
+                const bool first = d < rhalf;
+                const int i = first ? d : d - rhalf;
+                r = __float2half_rn(rope_elem(__half2float(kn[d]), __half2float(kn[first ? d + rhalf : d - rhalf]),
+                                              cs[i], first));
+            } else {
+                r = kn[d];
+            }
+            kd[d] = r;
+            vd[d] = vn[d];
+        }
+        if (p.q_rot_out) {
+            for (int hh = 0; hh < p.G; ++hh) {
+                const int hq = h * p.G + hh;
+                const __half* qr = p.q + (int64_t)b * p.q_sb + (int64_t)hq * p.q_sh;
+                __half* qo = p.q_rot_out + ((int64_t)b * p.Hq + hq) * D;
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const int d = lane * E + e;
+                    if (d < rot) {
+                        const bool first = d < rhalf;
+                        const int i = first ? d : d - rhalf;
+                        qo[d] = __float2half_rn(rope_elem(__half2float(qr[d]),
+                                                          __half2float(qr[first ? d + rhalf : d - rhalf]), cs[i], first));
+                    } else {
+                        qo[d] = qr[d];
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (p.advance && tid == 0) p.seq_lens[b] = si.T + 1;
+}
+
+// ------------------------------------------------------------------ host side
+
+static Tuning g_tuning;
+
+Tuning& tuning() { return g_tuning; }
+
+int device_sm_count(int dev) {
+    static std::mutex mu;
+    static int cache[128] = {0};
+    if (dev < 0 || dev >= 128) return 0;
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }();
+    return fn;
+}
+
+// 4-D map (head_dim, token, kv head, sequence) over an fp16 arena; 64 x 16 boxes,
+// 128-byte swizzle. Strides in elements.
+static int encode_kv_map(CUtensorMap* map, const void* base, int D, int64_t tokens, int Hkv, int Bdim, int64_t st,
+                         int64_t sh, int64_t sb) {
+    auto fn = encode_fn();
+    if (!fn) return FCCI_ETMAP;
+    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)tokens, (cuuint64_t)Hkv, (cuuint64_t)Bdim};
+    int64_t sbytes[3] = {st * 2, sh * 2, sb * 2};
+    // a stride of an extent-1 dimension is never used; give it a legal value
+    int64_t prev = (int64_t)D * 2;
+    for (int i = 0; i < 3; ++i) {
+        if (dims[i + 1] == 1) sbytes[i] = ((prev * (int64_t)dims[i] + 15) / 16) * 16;
+        prev = sbytes[i];
+    }
+    cuuint64_t strides[3] = {(cuuint64_t)sbytes[0], (cuuint64_t)sbytes[1], (cuuint64_t)sbytes[2]};
+    cuuint32_t box[4] = {64, (cuuint32_t)kGroupKeys, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FCCI_OK : FCCI_ETMAP;
+}
+
+WorkspaceLayout workspace_layout(int B, int Hq, int Hkv, int D, int grid) {
+    WorkspaceLayout w;
+    const int G = Hq / (Hkv > 0 ? Hkv : 1);
+    const size_t P = (size_t)B * Hkv;
+    const size_t slots = P + (size_t)grid;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    w.err = 0;
+    w.done = 4;
+    w.pair_cnt = 256;
+    w.part_lse = w.pair_cnt + up(P * 4);
+    w.part_o = w.part_lse + up(slots * G * 4);
+    w.total = w.part_o + up(slots * G * (size_t)D * 4);
+    w.zero_bytes = w.part_lse;  // header + counters
+    return w;
+}
+
+int max_grid(int dev) { return device_sm_count(dev) * kMaxCtasPerSm; }
+
+template <int D, int NB>
+static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUtensorMap& mv, int grid, cudaStream_t st,
+                           int dev) {
+    using LY = Layout<D, NB>;
+    static std::once_flag flags[128];
+    static cudaError_t attr_err[128];
+    if (dev < 0 || dev >= 128) return FCCI_EINVAL;
+    std::call_once(flags[dev], [&]() {
+        attr_err[dev] = cudaFuncSetAttribute(decode_attn_kernel<D, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024);
+    });
+    if (attr_err[dev] != cudaSuccess) return set_cuda_status(attr_err[dev]);
+    const size_t smem = LY::smem_bytes(prm.stages, prm.B, prm.split != 0);
+    decode_attn_kernel<D, NB><<<grid, kThreads, smem, st>>>(mk, mv, prm);
+    count_launch();
+    return set_cuda_status(cudaGetLastError());
+}
+
+static int pick_stages(int D, int NB, int B, bool split) {
+    auto fixed = [&](int s) -> size_t {
+        switch (D * 10 + NB) {
+            case 641: return Layout<64, 1>::smem_bytes(s, B, split);
+            case 642: return Layout<64, 2>::smem_bytes(s, B, split);
+            case 1281: return Layout<128, 1>::smem_bytes(s, B, split);
+            case 1282: return Layout<128, 2>::smem_bytes(s, B, split);
+            case 2561: return Layout<256, 1>::smem_bytes(s, B, split);
+            default: return (size_t)1 << 40;
+        }
+    };
+    const size_t budget = (size_t)(227 * 1024) / (size_t)(g_tuning.ctas_per_sm > 0 ? g_tuning.ctas_per_sm : 1);
+    int s = g_tuning.stages > 0 ? g_tuning.stages : 4;
+    while (s >= 2 && fixed(s) > budget) --s;
+    return s >= 2 ? s : 0;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int fill_params(const fcci_decode_desc* d, Params& p, bool attention) {
+    if (!d || d->abi_version != FCCI_DECODE_ABI_VERSION) return FCCI_EINVAL;
+    if (d->B <= 0 || d->Hq <= 0 || d->Hkv <= 0 || d->Hq % d->Hkv != 0) return FCCI_EINVAL;
+    if (d->D != 64 && d->D != 128 && d->D != 256) return FCCI_EUNSUPPORTED;
+    if (!d->q || !d->k_cache || !d->v_cache) return FCCI_EINVAL;
+    if (attention && !d->out) return FCCI_EINVAL;
+    if ((d->k_new == nullptr) != (d->v_new == nullptr)) return FCCI_EINVAL;
+    if (!attention && !d->k_new) return FCCI_EINVAL;
+    if (d->capacity <= 0) return FCCI_EINVAL;
+    if (d->rotary_dim < 0 || d->rotary_dim > d->D || (d->rotary_dim & 1)) return FCCI_EINVAL;
+    if (d->advance && !d->seq_lens) return FCCI_EINVAL;
+    if (!d->seq_lens && d->fixed_len < 0) return FCCI_EINVAL;
+    if (attention) {
+        if (!aligned16(d->k_cache) || !aligned16(d->v_cache)) return FCCI_EINVAL;
+        const int64_t ks[6] = {d->k_stride_t, d->k_stride_h, d->k_stride_b, d->v_stride_t, d->v_stride_h, d->v_stride_b};
+        for (int i = 0; i < 6; ++i)
+            if (ks[i] < 0 || (ks[i] & 7)) return FCCI_EINVAL;
+        if (d->k_stride_t == 0 || d->v_stride_t == 0) return FCCI_EINVAL;
+        if ((reinterpret_cast<uintptr_t>(d->out) & 3) || (d->out_stride_h & 1) || (d->out_stride_b & 1)) return FCCI_EINVAL;
+    }
+    const int E = d->D / 32;
+    if (d->k_new) {
+        // append path stores E contiguous halves per lane
+        const uintptr_t a = (uintptr_t)2 * E - 1;
+        if (((uintptr_t)d->k_cache & a) || ((uintptr_t)d->v_cache & a) || (d->k_stride_t * 2 & (int64_t)a) ||
+            (d->k_stride_h * 2 & (int64_t)a) || (d->k_stride_b * 2 & (int64_t)a) || (d->v_stride_t * 2 & (int64_t)a) ||
+            (d->v_stride_h * 2 & (int64_t)a) || (d->v_stride_b * 2 & (int64_t)a))
+            return FCCI_EINVAL;
+    }
+    memset(&p, 0, sizeof(p));
+    p.q = static_cast<const __half*>(d->q);
+    p.q_sb = d->q_stride_b;
+    p.q_sh = d->q_stride_h;
+    p.k_new = static_cast<const __half*>(d->k_new);
+    p.kn_sb = d->k_new_stride_b;
+    p.kn_sh = d->k_new_stride_h;
+    p.v_new = static_cast<const __half*>(d->v_new);
+    p.vn_sb = d->v_new_stride_b;
+    p.vn_sh = d->v_new_stride_h;
+    p.k_cache = static_cast<__half*>(d->k_cache);
+    p.k_sb = d->k_stride_b;
+    p.k_sh = d->k_stride_h;
+    p.k_st = d->k_stride_t;
+    p.v_cache = static_cast<__half*>(d->v_cache);
+    p.v_sb = d->v_stride_b;
+    p.v_sh = d->v_stride_h;
+    p.v_st = d->v_stride_t;
+    p.capacity = d->capacity;
+    p.cu_seqlens = d->cu_seqlens;
+    p.seq_lens = d->seq_lens;
+    p.fixed_len = d->fixed_len;
+    p.out = static_cast<__half*>(d->out);
+    p.o_sb = d->out_stride_b;
+    p.o_sh = d->out_stride_h;
+    p.q_rot_out = static_cast<__half*>(d->q_rot_out);
+    p.scale_log2 = d->scale * 1.4426950408889634f;
+    p.rope_theta = d->rope_theta;
+    p.rotary_dim = d->rotary_dim;
+    p.advance = d->advance;
+    p.append = d->k_new ? 1 : 0;
+    p.split = d->split ? 1 : 0;
+    p.B = d->B;
+    p.Hq = d->Hq;
+    p.Hkv = d->Hkv;
+    p.G = d->Hq / d->Hkv;
+    return FCCI_OK;
+}
+
+static void bind_workspace(Params& p, void* ws, const WorkspaceLayout& L) {
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    p.err = reinterpret_cast<uint32_t*>(base + L.err);
+    p.done_cnt = reinterpret_cast<uint32_t*>(base + L.done);
+    p.pair_cnt = reinterpret_cast<uint32_t*>(base + L.pair_cnt);
+    p.part_lse = reinterpret_cast<float*>(base + L.part_lse);
+    p.part_o = reinterpret_cast<float*>(base + L.part_o);
+}
+
+int decode_attention(const fcci_decode_desc* d, cudaStream_t stream) {
+    Params p;
+    int rc = fill_params(d, p, true);
+    if (rc) return set_status(rc, "fcci_decode_attention: invalid descriptor");
+    const int G = p.G;
+    const int NB = G <= 8 ? 1 : (G <= 16 ? 2 : 0);
+    if (NB == 0 || (d->D == 256 && NB == 2))
+        return set_status(FCCI_EUNSUPPORTED, "fcci_decode_attention: query group size unsupported");
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_status(cudaGetLastError());
+    const int sms = device_sm_count(dev);
+    if (sms <= 0) return set_status(FCCI_ECUDA, "fcci_decode_attention: no device");
+    const bool split = p.split != 0;
+    const int64_t pairs = (int64_t)p.B * p.Hkv;
+    int grid;
+    if (split) {
+        grid = sms * (g_tuning.ctas_per_sm > 0 ? g_tuning.ctas_per_sm : 1);
+        if (grid > sms * kMaxCtasPerSm) grid = sms * kMaxCtasPerSm;
+    } else {
+        if (pairs > 0x7fffffff) return set_status(FCCI_EINVAL, "fcci_decode_attention: too many pairs");
+        grid = (int)pairs;
+    }
+    const bool need_ws = split || p.advance;
+    if (need_ws) {
+        const WorkspaceLayout L = workspace_layout(p.B, p.Hq, p.Hkv, d->D, sms * kMaxCtasPerSm);
+        if (!d->workspace || d->workspace_bytes < L.total)
+            return set_status(FCCI_EWORKSPACE, "fcci_decode_attention: workspace missing or too small");
+        bind_workspace(p, d->workspace, L);
+    } else if (d->workspace) {
+        const WorkspaceLayout L = workspace_layout(p.B, p.Hq, p.Hkv, d->D, sms * kMaxCtasPerSm);
+        if (d->workspace_bytes >= L.total) bind_workspace(p, d->workspace, L);
+    }
+    p.stages = pick_stages(d->D, NB, p.B, split);
+    if (p.stages == 0) return set_status(FCCI_EUNSUPPORTED, "fcci_decode_attention: batch too large for shared memory");
+
+    CUtensorMap mk, mv;
+    const int Bdim = p.cu_seqlens ? 1 : p.B;
+    rc = encode_kv_map(&mk, p.k_cache, d->D, p.capacity, p.Hkv, Bdim, p.k_st, p.k_sh, p.k_sb);
+    if (!rc) rc = encode_kv_map(&mv, p.v_cache, d->D, p.capacity, p.Hkv, Bdim, p.v_st, p.v_sh, p.v_sb);
+    if (rc) return set_status(rc, "fcci_decode_attention: cuTensorMapEncodeTiled rejected the arena layout");
+
+    switch (d->D * 10 + NB) {
+        case 641: return launch_decode_t<64, 1>(p, mk, mv, grid, stream, dev);
+        case 642: return launch_decode_t<64, 2>(p, mk, mv, grid, stream, dev);
+        case 1281: return launch_decode_t<128, 1>(p, mk, mv, grid, stream, dev);
+        case 1282: return launch_decode_t<128, 2>(p, mk, mv, grid, stream, dev);
+        case 2561: return launch_decode_t<256, 1>(p, mk, mv, grid, stream, dev);
+        default: return set_status(FCCI_EUNSUPPORTED, "fcci_decode_attention: unsupported head_dim");
+    }
+}
+
+int rope_append(const fcci_decode_desc* d, cudaStream_t stream) {
+    Params p;
+    int rc = fill_params(d, p, false);
+    if (rc) return set_status(rc, "fcci_rope_append: invalid descriptor");
+    if (d->workspace) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const WorkspaceLayout L = workspace_layout(p.B, p.Hq, p.Hkv, d->D, max_grid(dev));
+        if (d->workspace_bytes >= L.total) bind_workspace(p, d->workspace, L);
+    }
+    switch (d->D) {
+        case 64: rope_append_kernel<64><<<p.B, 128, 0, stream>>>(p); break;
+        case 128: rope_append_kernel<128><<<p.B, 128, 0, stream>>>(p); break;
+        case 256: rope_append_kernel<256><<<p.B, 128, 0, stream>>>(p); break;
+        default: return set_status(FCCI_EUNSUPPORTED, "fcci_rope_append: unsupported head_dim");
+    }
+    count_launch();
+    return set_cuda_status(cudaGetLastError());
+}
+
+}  // namespace fcci

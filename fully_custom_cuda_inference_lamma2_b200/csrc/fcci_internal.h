@@ -1,0 +1,34 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "fcci_decode.h"
+
+namespace fcci {
+
+// Upper bound of resident decode CTAs per SM; the split-mode workspace is sized for it.
+constexpr int kMaxCtasPerSm = 2;
+
+struct Tuning {
+    int stages = 4;       // pipeline depth (64-key K+V tiles in flight per CTA)
+    int ctas_per_sm = 1;  // persistent CTAs per SM in split mode
+};
+Tuning& tuning();
+
+struct WorkspaceLayout {
+    size_t err, done, pair_cnt, part_lse, part_o, total, zero_bytes;
+};
+WorkspaceLayout workspace_layout(int B, int Hq, int Hkv, int D, int grid);
+int max_grid(int dev);
+int device_sm_count(int dev);
+
+int set_status(int code, const char* msg);
+int set_cuda_status(cudaError_t e);
+void count_launch();
+
+int decode_attention(const fcci_decode_desc* d, cudaStream_t stream);
+int rope_append(const fcci_decode_desc* d, cudaStream_t stream);
+
+}  // namespace fcci

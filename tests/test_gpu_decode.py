@@ -1,0 +1,288 @@
+"""GPU parity of the decode-attention path against the fp32 oracle.
+
+Tolerances: ctx within max-abs 2e-3 and relative-L2 1e-3 of the fp32 oracle
+(fp16 inputs and output); rotated q and appended K rows within 1 fp16 ulp of
+the oracle's fp16 rounding (sin/cos/pow of the CPU and GPU libraries may differ
+in the last fp32 bit); appended V rows and untouched arena rows bit-exact.
+"""
+import math
+
+import pytest
+import torch
+
+from helpers import fp16_ulp_diff, randn_half
+from oracle import decode_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def av():
+    import fully_custom_cuda_inference_lamma2_b200 as pkg
+
+    return pkg.attn_varlen
+
+
+def assert_close(got, want, what=""):
+    max_abs, rel = O.compare(got.float().cpu(), want)
+    assert max_abs <= O.MAX_ABS_TOL and rel <= O.REL_L2_TOL, f"{what}: max_abs={max_abs:.3g} rel_l2={rel:.3g}"
+
+
+# ------------------------------------------------------------------ forward (reference surface)
+
+@pytest.mark.parametrize("T", [1, 2, 63, 64, 65, 513, 4097])
+def test_forward_matches_oracle(av, T):
+    H, D = 32, 128
+    q = randn_half((H, D), 1)
+    k = randn_half((H, T, D), 2)
+    v = randn_half((H, T, D), 3)
+    scale = 1.0 / math.sqrt(D)
+    ctx = av.forward(q.to(DEV), k.to(DEV), v.to(DEV), T, scale)
+    torch.cuda.synchronize()
+    assert ctx.shape == (H, D) and ctx.dtype == torch.float16
+    assert_close(ctx, O.attn_varlen_forward(q, k, v, T, scale), f"T={T}")
+
+
+@pytest.mark.parametrize("D", [64, 256])
+def test_forward_head_dims(av, D):
+    H, T = 8, 300
+    q, k, v = randn_half((H, D), 4), randn_half((H, T, D), 5), randn_half((H, T, D), 6)
+    scale = 1.0 / math.sqrt(D)
+    ctx = av.forward(q.to(DEV), k.to(DEV), v.to(DEV), T, scale)
+    assert_close(ctx, O.attn_varlen_forward(q, k, v, T, scale), f"D={D}")
+
+
+def test_forward_honours_strides_and_seq_len(av):
+    # a slice of an arena [H, max_len, D]: row stride D, head stride max_len*D,
+    # attended over seq_len < k.size(1) (the reference needed exact copies here)
+    H, D, max_len, T, seq_len = 16, 128, 1024, 700, 333
+    arena_k = randn_half((H, max_len, D), 7)
+    arena_v = randn_half((H, max_len, D), 8)
+    q = randn_half((H, D), 9)
+    k = arena_k.to(DEV)[:, :T]
+    v = arena_v.to(DEV)[:, :T]
+    assert not k.is_contiguous()
+    ctx = av.forward(q.to(DEV), k, v, seq_len, 0.0883883)
+    assert_close(ctx, O.attn_varlen_forward(q, arena_k[:, :T], arena_v[:, :T], seq_len, 0.0883883), "strided")
+
+
+def test_forward_out_no_alloc_with_workspace(av):
+    H, D, T = 32, 128, 2000
+    q, k, v = randn_half((H, D), 10).to(DEV), randn_half((H, T, D), 11).to(DEV), randn_half((H, T, D), 12).to(DEV)
+    out = torch.empty(H, D, dtype=torch.float16, device=DEV)
+    ws = av.make_workspace(1, H, H, D)
+    av.forward_out(q, k, v, T, 0.0883883, out, ws)  # warm up (first launch sets kernel attributes)
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    av.forward_out(q, k, v, T, 0.0883883, out, ws)
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == before
+    assert_close(out, O.attn_varlen_forward(q.cpu(), k.cpu(), v.cpu(), T, 0.0883883), "forward_out")
+
+
+def test_forward_rejects_bad_inputs(av):
+    q = torch.zeros(4, 128, dtype=torch.float16, device=DEV)
+    k = torch.zeros(4, 10, 128, dtype=torch.float16, device=DEV)
+    with pytest.raises(RuntimeError, match="invalid seq_len"):
+        av.forward(q, k, k, 11, 1.0)
+    with pytest.raises(RuntimeError, match="invalid seq_len"):
+        av.forward(q, k, k, 0, 1.0)
+    with pytest.raises(RuntimeError, match="fp16"):
+        av.forward(q.float(), k, k, 5, 1.0)
+    with pytest.raises(RuntimeError, match="head mismatch"):
+        av.forward(q[:3], k, k, 5, 1.0)
+    with pytest.raises(RuntimeError, match="must be CUDA"):
+        av.forward(q.cpu(), k, k, 5, 1.0)
+
+
+# ------------------------------------------------------------------ batched / varlen decode step
+
+def make_case(B, Hkv, G, D, lens, cap, seed, packed=False, slack=5):
+    """Seeded decode inputs; rows past each sequence's T are NaN so any leak shows."""
+    Hq = Hkv * G
+    q = randn_half((B, Hq, D), seed)
+    k_new = randn_half((B, Hkv, D), seed + 1)
+    v_new = randn_half((B, Hkv, D), seed + 2)
+    if packed:
+        caps = [t + 1 + slack for t in lens]
+        cu = torch.tensor([0] + list(torch.tensor(caps).cumsum(0)), dtype=torch.int32)
+        total = int(cu[-1])
+        kc = randn_half((Hkv, total, D), seed + 3)
+        vc = randn_half((Hkv, total, D), seed + 4)
+        for b, t in enumerate(lens):
+            kc[:, int(cu[b]) + t:int(cu[b + 1])] = float("nan")
+            vc[:, int(cu[b]) + t:int(cu[b + 1])] = float("nan")
+    else:
+        cu = None
+        kc = randn_half((B, Hkv, cap, D), seed + 3)
+        vc = randn_half((B, Hkv, cap, D), seed + 4)
+        for b, t in enumerate(lens):
+            kc[b, :, t:] = float("nan")
+            vc[b, :, t:] = float("nan")
+    return q, k_new, v_new, kc, vc, torch.tensor(lens, dtype=torch.int32), cu
+
+
+def run_decode(av, q, k_new, v_new, kc, vc, lens, cu, *, split=True, advance=True, q_rot=True):
+    B, Hq, D = q.shape
+    dk, dv = kc.to(DEV), vc.to(DEV)
+    dlens = lens.to(DEV)
+    out = torch.full((B, Hq, D), float("nan"), dtype=torch.float16, device=DEV)
+    qr = torch.empty_like(q, device=DEV) if q_rot else None
+    ws = av.make_workspace(B, Hq, kc.shape[1] if cu is None else kc.shape[0], D)
+    av.decode(q.to(DEV), dk, dv, out, k_new=k_new.to(DEV) if k_new is not None else None,
+              v_new=v_new.to(DEV) if v_new is not None else None, seq_lens=dlens,
+              cu_seqlens=cu.to(DEV) if cu is not None else None, advance=advance, workspace=ws,
+              q_rot_out=qr, split=split)
+    torch.cuda.synchronize()
+    err = av.read_error(ws)
+    return dict(out=out.cpu(), q_rot=qr.cpu() if qr is not None else None, k=dk.cpu(), v=dv.cpu(),
+                lens=dlens.cpu(), err=err)
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("split", [True, False])
+def test_decode_batched_append_gqa(av, G, split):
+    B, Hkv, D, cap = 4, 2, 128, 400
+    lens = [0, 70, 255, 398]
+    q, kn, vn, kc, vc, T, cu = make_case(B, Hkv, G, D, lens, cap, seed=100 + G)
+    got = run_decode(av, q, kn, vn, kc, vc, T, cu, split=split)
+    want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn)
+    assert got["err"] == 0
+    assert_close(got["out"], want["ctx"], f"G={G} split={split}")
+    assert fp16_ulp_diff(got["q_rot"], want["q_rot"]) <= 1
+    for b, t in enumerate(lens):
+        assert fp16_ulp_diff(got["k"][b, :, t], want["k_cache"][b, :, t]) <= 1
+        assert torch.equal(got["v"][b, :, t], want["v_cache"][b, :, t])
+        assert torch.equal(got["k"][b, :, :t], kc[b, :, :t])  # cached rows untouched
+    assert got["lens"].tolist() == [t + 1 for t in lens]
+
+
+@pytest.mark.parametrize("split", [True, False])
+def test_decode_packed_varlen(av, split):
+    # ragged lengths including the one-key sequence (T=0) and tile edges
+    lens = [0, 1, 15, 16, 17, 63, 64, 65, 127, 128, 129, 1000, 3]
+    B, Hkv, G, D = len(lens), 4, 8, 128
+    q, kn, vn, kc, vc, T, cu = make_case(B, Hkv, G, D, lens, None, seed=200, packed=True)
+    got = run_decode(av, q, kn, vn, kc, vc, T, cu, split=split)
+    want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn, cu_seqlens=cu)
+    assert got["err"] == 0
+    assert_close(got["out"], want["ctx"], f"packed split={split}")
+    assert fp16_ulp_diff(got["q_rot"], want["q_rot"]) <= 1
+    for b, t in enumerate(lens):
+        row = int(cu[b]) + t
+        assert fp16_ulp_diff(got["k"][:, row], want["k_cache"][:, row]) <= 1
+        assert torch.equal(got["v"][:, row], want["v_cache"][:, row])
+    assert got["lens"].tolist() == [t + 1 for t in lens]
+
+
+def test_decode_attention_only(av):
+    # no append: attend to the first T_b keys with q as given (no RoPE)
+    lens = [1, 64, 500, 77]
+    B, Hkv, G, D, cap = 4, 8, 8, 128, 512
+    q, _, _, kc, vc, T, cu = make_case(B, Hkv, G, D, lens, cap, seed=300)
+    got = run_decode(av, q, None, None, kc, vc, T, cu, advance=False, q_rot=False)
+    want = O.decode_step(q, kc, vc, T)
+    assert got["err"] == 0
+    assert_close(got["out"], want["ctx"], "attention-only")
+    assert got["lens"].tolist() == lens
+
+
+def test_decode_long_split_kv(av):
+    # one long sequence per kv head pair: the stream-K split cuts every pair
+    lens = [32768, 20000]
+    B, Hkv, G, D, cap = 2, 8, 8, 128, 32800
+    q, kn, vn, kc, vc, T, cu = make_case(B, Hkv, G, D, lens, cap, seed=400)
+    got = run_decode(av, q, kn, vn, kc, vc, T, cu)
+    want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn)
+    assert got["err"] == 0
+    assert_close(got["out"], want["ctx"], "split-kv 32k")
+
+
+def test_decode_capacity_overflow_sets_error(av):
+    lens = [10, 400, 20]  # 400 + 1 > cap 400
+    B, Hkv, G, D, cap = 3, 2, 4, 128, 400
+    q, kn, vn, kc, vc, T, cu = make_case(B, Hkv, G, D, lens, cap, seed=500)
+    got = run_decode(av, q, kn, vn, kc, vc, T, cu)
+    assert got["err"] & 1
+    want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn)
+    assert not bool(want["ok"][1])
+    assert torch.count_nonzero(got["out"][1]) == 0
+    assert_close(got["out"][[0, 2]], want["ctx"][[0, 2]], "valid sequences")
+    assert got["lens"].tolist() == [11, 400, 21]
+
+
+@pytest.mark.parametrize("rotary_dim", [0, 64])
+def test_decode_partial_rotary(av, rotary_dim):
+    lens = [5, 300]
+    B, Hkv, G, D, cap = 2, 2, 4, 128, 320
+    q, kn, vn, kc, vc, T, cu = make_case(B, Hkv, G, D, lens, cap, seed=600)
+    dk, dv = kc.to(DEV), vc.to(DEV)
+    out = torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV)
+    av.decode(q.to(DEV), dk, dv, out, k_new=kn.to(DEV), v_new=vn.to(DEV), seq_lens=T.to(DEV),
+              rotary_dim=rotary_dim, rope_theta=500000.0)
+    want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn, rotary_dim=rotary_dim, theta=500000.0)
+    assert_close(out, want["ctx"], f"rotary_dim={rotary_dim}")
+
+
+def test_rope_append_standalone(av):
+    lens = [0, 9, 130]
+    B, Hkv, G, D, cap = 3, 4, 2, 128, 200
+    q, kn, vn, kc, vc, T, cu = make_case(B, Hkv, G, D, lens, cap, seed=700)
+    dk, dv, dT = kc.to(DEV), vc.to(DEV), T.to(DEV)
+    qr = torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV)
+    av.rope_append(q.to(DEV), kn.to(DEV), vn.to(DEV), dk, dv, dT, advance=True, q_rot_out=qr)
+    want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn)
+    assert fp16_ulp_diff(qr.cpu(), want["q_rot"]) <= 1
+    for b, t in enumerate(lens):
+        assert fp16_ulp_diff(dk.cpu()[b, :, t], want["k_cache"][b, :, t]) <= 1
+        assert torch.equal(dv.cpu()[b, :, t], want["v_cache"][b, :, t])
+    assert dT.cpu().tolist() == [t + 1 for t in lens]
+
+
+def test_decode_graph_replays_across_lengths(av):
+    """One CUDA graph serves every length: capture once, replay as T grows, no allocation."""
+    B, Hkv, G, D, cap = 3, 2, 8, 128, 300
+    lens = [40, 120, 7]
+    _, _, _, kc, vc, T, _ = make_case(B, Hkv, G, D, lens, cap, seed=800)
+    dk, dv, dT = kc.to(DEV), vc.to(DEV), T.to(DEV)
+    sq = torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV)
+    skn = torch.empty(B, Hkv, D, dtype=torch.float16, device=DEV)
+    svn = torch.empty_like(skn)
+    out = torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV)
+    ws = av.make_workspace(B, Hkv * G, Hkv, D)
+    # warm-up outside capture on a scratch copy, then restore
+    av.decode(sq, dk.clone(), dv.clone(), out, k_new=skn, v_new=svn, seq_lens=dT.clone(), advance=True, workspace=ws)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            av.decode(sq, dk, dv, out, k_new=skn, v_new=svn, seq_lens=dT, advance=True, workspace=ws)
+    torch.cuda.synchronize()
+    ref_k, ref_v, ref_T = kc.clone(), vc.clone(), T.clone()
+    mem0 = torch.cuda.memory_allocated()
+    for step in range(4):
+        q = randn_half((B, Hkv * G, D), 900 + step)
+        kn = randn_half((B, Hkv, D), 950 + step)
+        vn = randn_half((B, Hkv, D), 980 + step)
+        sq.copy_(q)
+        skn.copy_(kn)
+        svn.copy_(vn)
+        g.replay()
+        torch.cuda.synchronize()
+        want = O.decode_step(q, ref_k, ref_v, ref_T, k_new=kn, v_new=vn)
+        assert_close(out.cpu(), want["ctx"], f"replay {step}")
+        ref_k, ref_v, ref_T = want["k_cache"], want["v_cache"], want["seq_lens"]
+        assert dT.cpu().tolist() == ref_T.tolist()
+    assert torch.cuda.memory_allocated() == mem0
+    assert av.read_error(ws) == 0
+
+
+def test_nan_past_end_does_not_leak(av):
+    # every row past T is NaN (make_case); the output must be finite everywhere
+    lens = [3, 17, 200]
+    q, kn, vn, kc, vc, T, cu = make_case(3, 2, 8, 128, lens, 256, seed=1000)
+    got = run_decode(av, q, kn, vn, kc, vc, T, cu)
+    assert torch.isfinite(got["out"].float()).all()

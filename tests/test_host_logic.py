@@ -1,0 +1,84 @@
+"""CPU model of the kernel's work decomposition and of the multi-GPU partitions.
+
+The decode kernel (decode_attn.cu) cuts every (sequence, kv head) pair into
+64-key tiles, gives CTA c the tiles [c*N/C, (c+1)*N/C) of the concatenated line,
+and stores the partial of pair p computed by CTA c in slot p + c. These tests
+restate that arithmetic and check its invariants on random length mixes."""
+import random
+
+import pytest
+
+from fully_custom_cuda_inference_lamma2_b200 import sharding
+
+TILE = 64
+
+
+def tiles_of(L):
+    return (L + TILE - 1) // TILE if L > 0 else 1
+
+
+def cta_of_tile(t, N, C):
+    return ((t + 1) * C + N - 1) // N - 1
+
+
+def decompose(lens, Hkv, C):
+    """(pairs, N) where pairs[p] = (first_tile, n_tiles), p = b*Hkv + h."""
+    pairs, t = [], 0
+    for L in lens:
+        n = tiles_of(L)
+        for _ in range(Hkv):
+            pairs.append((t, n))
+            t += n
+    return pairs, t
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_stream_k_ranges_slots_and_pieces(seed):
+    rnd = random.Random(seed)
+    B = rnd.randint(1, 70)
+    Hkv = rnd.choice([1, 2, 8, 32])
+    C = rnd.choice([1, 7, 148, 296])
+    lens = [rnd.choice([0, 1, 15, 64, 65, rnd.randint(1, 40000)]) for _ in range(B)]
+    pairs, N = decompose(lens, Hkv, C)
+    owner = {}
+    for c in range(C):
+        lo, hi = c * N // C, (c + 1) * N // C
+        for t in range(lo, hi):
+            assert t not in owner
+            owner[t] = c
+            assert cta_of_tile(t, N, C) == c
+    assert len(owner) == N
+    slots = set()
+    for p, (first, n) in enumerate(pairs):
+        c0, c1 = cta_of_tile(first, N, C), cta_of_tile(first + n - 1, N, C)
+        ctas = sorted({owner[t] for t in range(first, first + n)})
+        assert ctas == list(range(c0, c1 + 1))  # pieces = c1 - c0 + 1, contiguous
+        for c in ctas:
+            s = p + c
+            assert s not in slots and s < len(pairs) + C
+            slots.add(s)
+
+
+def test_partition_sequences_balances_bytes():
+    rnd = random.Random(3)
+    lens = [rnd.randint(128, 8192) for _ in range(64)]
+    for n in (1, 2, 4, 8):
+        parts = sharding.partition_sequences(lens, n)
+        assert sorted(i for p in parts for i in p) == list(range(64))
+        loads = [sum(lens[i] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= max(lens)
+        assert parts == sharding.partition_sequences(lens, n)  # deterministic
+
+
+def test_partition_kv_heads():
+    assert sharding.partition_kv_heads(8, 64, 8, 3) == (3, 4, 24, 32)
+    assert sharding.partition_kv_heads(8, 64, 2, 1) == (4, 8, 32, 64)
+    with pytest.raises(ValueError):
+        sharding.partition_kv_heads(8, 64, 3, 0)
+
+
+def test_partition_by_cost_prefill():
+    lens = [256, 4096, 1000, 3000, 500]
+    parts = sharding.partition_by_cost([L * (L + 1) / 2 for L in lens], 2)
+    assert sorted(i for p in parts for i in p) == list(range(5))
+    assert 1 in parts[0]  # the longest goes first to rank 0
