@@ -246,10 +246,14 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     // ---- this CTA's tile range
     long long t_begin = 0, t_end = 0, N = 0;
     int b0 = 0, h0 = 0, j0 = 0;
+    long long C = gridDim.x;  // CTAs that take tiles: never more than there are tiles
     if (p.split) {
         N = tile_base[B];
-        t_begin = (long long)blockIdx.x * N / gridDim.x;
-        t_end = ((long long)blockIdx.x + 1) * N / gridDim.x;
+        C = N < (long long)gridDim.x ? N : (long long)gridDim.x;
+        if ((long long)blockIdx.x < C) {
+            t_begin = (long long)blockIdx.x * N / C;
+            t_end = ((long long)blockIdx.x + 1) * N / C;
+        }
         if (t_begin < t_end) {
             int lo = 0, hi = B - 1;
             while (lo < hi) {
@@ -574,8 +578,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 int c0 = 0, c1 = 0;
                 if (p.split) {
                     const long long pfirst = tile_base[b] + (long long)h * tiles;
-                    c0 = cta_of_tile(pfirst, N, gridDim.x);
-                    c1 = cta_of_tile(pfirst + tiles - 1, N, gridDim.x);
+                    c0 = cta_of_tile(pfirst, N, C);
+                    c1 = cta_of_tile(pfirst + tiles - 1, N, C);
                     whole = (c0 == c1);
                 }
                 const int slot = pidx + blockIdx.x;
@@ -783,8 +787,8 @@ static int encode_kv_map(CUtensorMap* map, const void* base, int D, int64_t toke
     if (!fn) return FCCI_ETMAP;
     cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)tokens, (cuuint64_t)Hkv, (cuuint64_t)Bdim};
     int64_t sbytes[3] = {st * 2, sh * 2, sb * 2};
-    // a stride of an extent-1 dimension is never used; give it a legal value
-    int64_t prev = (int64_t)D * 2;
+    // a stride of an extent-1 dimension is never used; give it the packed value
+    int64_t prev = 2;  // bytes per element: the stride of dimension 0
     for (int i = 0; i < 3; ++i) {
         if (dims[i + 1] == 1) sbytes[i] = ((prev * (int64_t)dims[i] + 15) / 16) * 16;
         prev = sbytes[i];

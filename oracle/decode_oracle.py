@@ -32,20 +32,23 @@ from typing import Optional
 import torch
 
 
-def inv_freq(rotary_dim: int, theta: float) -> torch.Tensor:
+def inv_freq(rotary_dim: int, theta: float, device=None) -> torch.Tensor:
     """fp32 inverse frequencies theta ** (-i / half), i < half (driver :95-97)."""
     half = rotary_dim // 2
-    idx = torch.arange(half, dtype=torch.float32)
+    idx = torch.arange(half, dtype=torch.float32, device=device)
     return theta ** (-idx / float(half))
 
 
 def rope_rotate_half(x: torch.Tensor, pos: int, rotary_dim: int, theta: float = 10000.0) -> torch.Tensor:
-    """Rotate-half RoPE of x [n, D] at integer position pos; returns a new tensor of x's dtype."""
+    """Rotate-half RoPE of x [n, D] at integer position pos; returns a new tensor of x's dtype.
+
+    Evaluated on x's device, as the driver evaluates it on its own (CUDA) tensors, so a
+    CUDA input reproduces the reference's device arithmetic (its powf/cosf/sinf)."""
     out = x.clone()
     if rotary_dim <= 0:
         return out
     half = rotary_dim // 2
-    angle = pos * inv_freq(rotary_dim, theta).view(1, -1)
+    angle = pos * inv_freq(rotary_dim, theta, x.device).view(1, -1)
     cos, sin = torch.cos(angle), torch.sin(angle)
     x1 = x[:, :half].float()
     x2 = x[:, half:rotary_dim].float()

@@ -32,14 +32,19 @@ def decompose(lens, Hkv, C):
     return pairs, t
 
 
-@pytest.mark.parametrize("seed", range(20))
+@pytest.mark.parametrize("seed", range(40))
 def test_stream_k_ranges_slots_and_pieces(seed):
     rnd = random.Random(seed)
     B = rnd.randint(1, 70)
     Hkv = rnd.choice([1, 2, 8, 32])
-    C = rnd.choice([1, 7, 148, 296])
-    lens = [rnd.choice([0, 1, 15, 64, 65, rnd.randint(1, 40000)]) for _ in range(B)]
-    pairs, N = decompose(lens, Hkv, C)
+    grid = rnd.choice([1, 7, 148, 296])
+    if seed % 2:  # few tiles: fewer than CTAs
+        lens = [rnd.choice([0, 1, 15, 64, 65, 200]) for _ in range(rnd.randint(1, 4))]
+        B = len(lens)
+    else:
+        lens = [rnd.choice([0, 1, 15, 64, 65, rnd.randint(1, 40000)]) for _ in range(B)]
+    pairs, N = decompose(lens, Hkv, grid)
+    C = min(grid, N)  # the kernel's effective grid: CTAs past N take no tiles
     owner = {}
     for c in range(C):
         lo, hi = c * N // C, (c + 1) * N // C
@@ -55,7 +60,7 @@ def test_stream_k_ranges_slots_and_pieces(seed):
         assert ctas == list(range(c0, c1 + 1))  # pieces = c1 - c0 + 1, contiguous
         for c in ctas:
             s = p + c
-            assert s not in slots and s < len(pairs) + C
+            assert s not in slots and s < len(pairs) + grid
             slots.add(s)
 
 
