@@ -107,8 +107,8 @@ int fcci_decode_read_error(void* workspace, uint32_t* flags, int clear, cudaStre
 int fcci_decode_set_tuning(int stages, int ctas_per_sm) {
     if (stages < 0 || stages > 8 || ctas_per_sm < 0 || ctas_per_sm > fcci::kMaxCtasPerSm)
         return fcci::set_status(FCCI_EINVAL, "fcci_decode_set_tuning: out of range");
-    if (stages) fcci::tuning().stages = stages;
-    if (ctas_per_sm) fcci::tuning().ctas_per_sm = ctas_per_sm;
+    fcci::tuning().stages = stages;
+    fcci::tuning().ctas_per_sm = ctas_per_sm;
     return fcci::set_status(FCCI_OK, nullptr);
 }
 

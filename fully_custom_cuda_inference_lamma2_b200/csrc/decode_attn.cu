@@ -144,15 +144,20 @@ __device__ __forceinline__ float rope_elem(float x, float partner, float2 cs, bo
                       : __fadd_rn(__fmul_rn(x, cs.x), __fmul_rn(partner, cs.y));
 }
 
+// Most CTAs that can hold pieces of one pair: the split grid never exceeds this.
+constexpr int kMaxPieces = 320;
+
 template <int D, int NB>
 struct Layout {
     static constexpr int G8 = 8 * NB;
     static constexpr int KT = 128 * D;  // bytes of one 64-key tile of K (or V)
     static constexpr int RP = D + 4;    // fp32 pitch of the cross-warp reduction rows
     static constexpr int QP = D + 8;    // fp16 pitch of the rotated-query rows
+    // cross-warp reduction rows; reused for the per-piece weights of a pair merge
+    static constexpr int RED = kConsumerWarps * G8 * RP > kMaxPieces * G8 ? kConsumerWarps * G8 * RP : kMaxPieces * G8;
     static __host__ __device__ constexpr size_t stage_bytes() { return 2 * (size_t)KT; }
     static __host__ __device__ constexpr size_t fixed_bytes(int stages) {
-        return (size_t)stages * stage_bytes() + sizeof(float) * kConsumerWarps * G8 * RP +
+        return (size_t)stages * stage_bytes() + sizeof(float) * RED +
                sizeof(float) * kConsumerWarps * G8 * 2 + sizeof(__half) * G8 * QP + sizeof(float2) * (D / 2) +
                sizeof(uint64_t) * 2 * stages + sizeof(int) * 8;
     }
@@ -179,7 +184,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     const int S = p.stages;
     uint8_t* stages = sm;
     float* red_acc = reinterpret_cast<float*>(stages + (size_t)S * LY::stage_bytes());
-    float* red_ml = red_acc + kConsumerWarps * G8 * RP;
+    float* red_ml = red_acc + LY::RED;
     __half* qrot = reinterpret_cast<__half*>(red_ml + kConsumerWarps * G8 * 2);
     float2* rope_cs = reinterpret_cast<float2*>(qrot + G8 * QP);
     uint64_t* full = reinterpret_cast<uint64_t*>(rope_cs + D / 2);
@@ -359,23 +364,33 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 }
                 const bool write_qrot = (p.q_rot_out != nullptr) && (j == 0);
                 const __half* qb = p.q + (int64_t)b * p.q_sb;
-                for (int e = ctid; e < G8 * D; e += kConsumerThreads) {
+                // all loads first (one L2 round trip), then rotate; element e -> (head, dim)
+                constexpr int NQ = G8 * D / kConsumerThreads;
+                __half qx[NQ], qp[NQ];
+#pragma unroll
+                for (int k = 0; k < NQ; ++k) {
+                    const int e = ctid + k * kConsumerThreads;
                     const int hh = e / D;
                     const int d = e - hh * D;
-                    __half val = __float2half_rn(0.f);
+                    qx[k] = qp[k] = __float2half_rn(0.f);
                     if (hh < G) {
                         const __half* qr = qb + (int64_t)(h * G + hh) * p.q_sh;
-                        if (d < rot) {
-                            const bool first = d < rhalf;
-                            const int i = first ? d : d - rhalf;
-                            const float x = __half2float(qr[d]);
-                            const float xp = __half2float(qr[first ? d + rhalf : d - rhalf]);
-                            val = __float2half_rn(rope_elem(x, xp, rope_cs[i], first));
-                        } else {
-                            val = qr[d];
-                        }
-                        if (write_qrot) p.q_rot_out[((int64_t)b * p.Hq + h * G + hh) * D + d] = val;
+                        qx[k] = qr[d];
+                        if (d < rot) qp[k] = qr[d < rhalf ? d + rhalf : d - rhalf];
                     }
+                }
+#pragma unroll
+                for (int k = 0; k < NQ; ++k) {
+                    const int e = ctid + k * kConsumerThreads;
+                    const int hh = e / D;
+                    const int d = e - hh * D;
+                    __half val = qx[k];
+                    if (hh < G && d < rot) {
+                        const bool first = d < rhalf;
+                        val = __float2half_rn(
+                            rope_elem(__half2float(qx[k]), __half2float(qp[k]), rope_cs[first ? d : d - rhalf], first));
+                    }
+                    if (write_qrot && hh < G) p.q_rot_out[((int64_t)b * p.Hq + h * G + hh) * D + d] = val;
                     qrot[hh * QP + d] = val;
                 }
                 named_bar_sync(kConsumerBar, kConsumerThreads);
@@ -621,28 +636,55 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     }
                     named_bar_sync(kConsumerBar, kConsumerThreads);
                     if (misc[1]) {
+                        // merge the pieces: lse of every piece into shared memory (parallel
+                        // loads), per-head weights, then the weighted sum of the partial o's
+                        // with several pieces' loads in flight per thread
                         __threadfence();
-                        for (int e = ctid * 2; e < G * D; e += 2 * kConsumerThreads) {
-                            const int hh = e / D;
-                            const int d = e - hh * D;
+                        const int nparts = c1 - c0 + 1;
+                        float* wts = red_acc;  // [nparts][G]; free after the segment merge above
+                        for (int idx = ctid; idx < nparts * G; idx += kConsumerThreads)
+                            wts[idx] = __ldcg(p.part_lse + (size_t)(pidx + c0) * G + idx);
+                        named_bar_sync(kConsumerBar, kConsumerThreads);
+                        for (int hh = ctid; hh < G; hh += kConsumerThreads) {
                             float LSE = -INFINITY;
-                            for (int c = c0; c <= c1; ++c)
-                                LSE = fmaxf(LSE, __ldcg(p.part_lse + (size_t)(pidx + c) * G + hh));
-                            float W = 0.f, o0 = 0.f, o1 = 0.f;
-                            if (LSE != -INFINITY) {
-                                for (int c = c0; c <= c1; ++c) {
-                                    const float wgt = ex2(__ldcg(p.part_lse + (size_t)(pidx + c) * G + hh) - LSE);
-                                    const float2 v =
-                                        __ldcg(reinterpret_cast<const float2*>(p.part_o + ((size_t)(pidx + c) * G + hh) * D + d));
-                                    W += wgt;
-                                    o0 += wgt * v.x;
-                                    o1 += wgt * v.y;
-                                }
+                            for (int c = 0; c < nparts; ++c) LSE = fmaxf(LSE, wts[c * G + hh]);
+                            float W = 0.f;
+                            for (int c = 0; c < nparts; ++c) {
+                                const float w = LSE == -INFINITY ? 0.f : ex2(wts[c * G + hh] - LSE);
+                                wts[c * G + hh] = w;
+                                W += w;
                             }
                             const float inv = W > 0.f ? 1.f / W : 0.f;
-                            *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) =
-                                __floats2half2_rn(o0 * inv, o1 * inv);
+                            for (int c = 0; c < nparts; ++c) wts[c * G + hh] *= inv;
                         }
+                        named_bar_sync(kConsumerBar, kConsumerThreads);
+                        const float* po = p.part_o + (size_t)(pidx + c0) * G * D;
+                        for (int e = ctid * 2; e < G * D; e += 2 * kConsumerThreads) {
+                            const int hh = e / D;
+                            float o0 = 0.f, o1 = 0.f;
+                            int c = 0;
+                            for (; c + 4 <= nparts; c += 4) {
+                                float2 v[4];
+#pragma unroll
+                                for (int u = 0; u < 4; ++u)
+                                    v[u] = __ldcg(reinterpret_cast<const float2*>(po + (size_t)(c + u) * G * D + e));
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) {
+                                    const float w = wts[(c + u) * G + hh];
+                                    o0 += w * v[u].x;
+                                    o1 += w * v[u].y;
+                                }
+                            }
+                            for (; c < nparts; ++c) {
+                                const float2 v = __ldcg(reinterpret_cast<const float2*>(po + (size_t)c * G * D + e));
+                                const float w = wts[c * G + hh];
+                                o0 += w * v.x;
+                                o1 += w * v.y;
+                            }
+                            const int d = e - hh * D;
+                            *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) = __floats2half2_rn(o0, o1);
+                        }
+                        named_bar_sync(kConsumerBar, kConsumerThreads);
                         if (ctid == 0) atomicExch(&p.pair_cnt[pidx], 0u);
                     }
                 }
@@ -745,7 +787,7 @@ __global__ void __launch_bounds__(128) rope_append_kernel(const Params p) {
 
 // ------------------------------------------------------------------ host side
 
-static Tuning g_tuning;
+static Tuning g_tuning;  // 0 = automatic
 
 Tuning& tuning() { return g_tuning; }
 
@@ -838,8 +880,15 @@ static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUten
     return set_cuda_status(cudaGetLastError());
 }
 
-static int pick_stages(int D, int NB, int B, bool split) {
-    auto fixed = [&](int s) -> size_t {
+// Launch shape: persistent CTAs per SM and pipeline stages per CTA. Two CTAs
+// per SM hide the consumers' per-tile latency (8 consumer warps per SM), so they
+// are preferred whenever two stages fit in half of the SM's shared memory.
+struct Shape {
+    int stages, ctas_per_sm;
+};
+
+static Shape pick_shape(int D, int NB, int B, bool split) {
+    auto bytes = [&](int s) -> size_t {
         switch (D * 10 + NB) {
             case 641: return Layout<64, 1>::smem_bytes(s, B, split);
             case 642: return Layout<64, 2>::smem_bytes(s, B, split);
@@ -849,10 +898,17 @@ static int pick_stages(int D, int NB, int B, bool split) {
             default: return (size_t)1 << 40;
         }
     };
-    const size_t budget = (size_t)(227 * 1024) / (size_t)(g_tuning.ctas_per_sm > 0 ? g_tuning.ctas_per_sm : 1);
-    int s = g_tuning.stages > 0 ? g_tuning.stages : 4;
-    while (s >= 2 && fixed(s) > budget) --s;
-    return s >= 2 ? s : 0;
+    const size_t sm_bytes = 228 * 1024, per_cta_reserved = 1024, cta_max = 227 * 1024;
+    const int want_stages = g_tuning.stages > 0 ? g_tuning.stages : 4;
+    for (int ctas = (g_tuning.ctas_per_sm > 0 ? g_tuning.ctas_per_sm : kMaxCtasPerSm); ctas >= 1; --ctas) {
+        size_t budget = sm_bytes / ctas - per_cta_reserved;
+        if (budget > cta_max) budget = cta_max;
+        int s = want_stages;
+        while (s >= 2 && bytes(s) > budget) --s;
+        if (s >= 2) return {s, ctas};
+        if (g_tuning.ctas_per_sm > 0) break;
+    }
+    return {0, 0};
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -948,10 +1004,13 @@ int decode_attention(const fcci_decode_desc* d, cudaStream_t stream) {
     if (sms <= 0) return set_status(FCCI_ECUDA, "fcci_decode_attention: no device");
     const bool split = p.split != 0;
     const int64_t pairs = (int64_t)p.B * p.Hkv;
+    const Shape shape = pick_shape(d->D, NB, p.B, split);
+    if (shape.stages == 0) return set_status(FCCI_EUNSUPPORTED, "fcci_decode_attention: batch too large for shared memory");
+    p.stages = shape.stages;
     int grid;
     if (split) {
-        grid = sms * (g_tuning.ctas_per_sm > 0 ? g_tuning.ctas_per_sm : 1);
-        if (grid > sms * kMaxCtasPerSm) grid = sms * kMaxCtasPerSm;
+        grid = sms * shape.ctas_per_sm;
+        if (grid > kMaxPieces) grid = kMaxPieces;
     } else {
         if (pairs > 0x7fffffff) return set_status(FCCI_EINVAL, "fcci_decode_attention: too many pairs");
         grid = (int)pairs;
@@ -966,8 +1025,6 @@ int decode_attention(const fcci_decode_desc* d, cudaStream_t stream) {
         const WorkspaceLayout L = workspace_layout(p.B, p.Hq, p.Hkv, d->D, sms * kMaxCtasPerSm);
         if (d->workspace_bytes >= L.total) bind_workspace(p, d->workspace, L);
     }
-    p.stages = pick_stages(d->D, NB, p.B, split);
-    if (p.stages == 0) return set_status(FCCI_EUNSUPPORTED, "fcci_decode_attention: batch too large for shared memory");
 
     CUtensorMap mk, mv;
     const int Bdim = p.cu_seqlens ? 1 : p.B;

@@ -12,8 +12,8 @@ namespace fcci {
 constexpr int kMaxCtasPerSm = 2;
 
 struct Tuning {
-    int stages = 4;       // pipeline depth (64-key K+V tiles in flight per CTA)
-    int ctas_per_sm = 1;  // persistent CTAs per SM in split mode
+    int stages = 0;       // pipeline depth (64-key K+V tiles per CTA); 0 = automatic
+    int ctas_per_sm = 0;  // persistent CTAs per SM in split mode; 0 = automatic
 };
 Tuning& tuning();
 

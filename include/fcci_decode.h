@@ -146,7 +146,7 @@ int fcci_decode_workspace_init(void* workspace, size_t bytes, cudaStream_t strea
 int fcci_decode_read_error(void* workspace, uint32_t* flags, int clear, cudaStream_t stream);
 
 /* Tuning hook for measurements: pipeline stages per CTA (2..8) and persistent
- * CTAs per SM (1..2) of the split mode; 0 keeps the current value. */
+ * CTAs per SM (1..2) of the split mode; 0 selects the automatic choice. */
 int fcci_decode_set_tuning(int stages, int ctas_per_sm);
 
 /* Status of the last call on this host thread, and its message. */
