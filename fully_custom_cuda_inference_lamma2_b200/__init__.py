@@ -35,7 +35,7 @@ try:
 except ImportError as exc:  # pragma: no cover - exercised only when unbuilt
     raise ImportError(
         "fully_custom_cuda_inference_lamma2_b200: native modules are not built; run "
-        "`python -m fully_custom_cuda_inference_lamma2_b200.build`"
+        "`python fully_custom_cuda_inference_lamma2_b200/build.py`"
     ) from exc
 
 from .arena import KVArena, decode_attention  # noqa: E402

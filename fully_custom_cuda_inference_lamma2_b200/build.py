@@ -5,7 +5,8 @@ Produces, next to this file:
   attn_varlen<ext-suffix>                    pybind module `attn_varlen`
   capture_decode_step<ext-suffix>            pybind module `capture_decode_step`
 
-Usage: python -m fully_custom_cuda_inference_lamma2_b200.build [--force]
+Usage: python fully_custom_cuda_inference_lamma2_b200/build.py [--force]
+(by path: importing the package requires the modules this script builds)
 Nothing is compiled when every output is newer than its sources.
 """
 from __future__ import annotations
