@@ -913,25 +913,32 @@ static Shape pick_shape(int D, int NB, int B, bool split) {
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Validates a descriptor; on failure records the reason (fcci_last_error_string)
+// and returns its FCCI_E* code.
 static int fill_params(const fcci_decode_desc* d, Params& p, bool attention) {
-    if (!d || d->abi_version != FCCI_DECODE_ABI_VERSION) return FCCI_EINVAL;
-    if (d->B <= 0 || d->Hq <= 0 || d->Hkv <= 0 || d->Hq % d->Hkv != 0) return FCCI_EINVAL;
-    if (d->D != 64 && d->D != 128 && d->D != 256) return FCCI_EUNSUPPORTED;
-    if (!d->q || !d->k_cache || !d->v_cache) return FCCI_EINVAL;
-    if (attention && !d->out) return FCCI_EINVAL;
-    if ((d->k_new == nullptr) != (d->v_new == nullptr)) return FCCI_EINVAL;
-    if (!attention && !d->k_new) return FCCI_EINVAL;
-    if (d->capacity <= 0) return FCCI_EINVAL;
-    if (d->rotary_dim < 0 || d->rotary_dim > d->D || (d->rotary_dim & 1)) return FCCI_EINVAL;
-    if (d->advance && !d->seq_lens) return FCCI_EINVAL;
-    if (!d->seq_lens && d->fixed_len < 0) return FCCI_EINVAL;
+    auto bad = [](int code, const char* why) { return set_status(code, why); };
+    if (!d) return bad(FCCI_EINVAL, "descriptor is NULL");
+    if (d->abi_version != FCCI_DECODE_ABI_VERSION) return bad(FCCI_EINVAL, "abi_version mismatch");
+    if (d->B <= 0 || d->Hq <= 0 || d->Hkv <= 0 || d->Hq % d->Hkv != 0)
+        return bad(FCCI_EINVAL, "B, Hq, Hkv must be positive and Hq a multiple of Hkv");
+    if (d->D != 64 && d->D != 128 && d->D != 256) return bad(FCCI_EUNSUPPORTED, "unsupported head_dim (64, 128 or 256)");
+    if (!d->q || !d->k_cache || !d->v_cache) return bad(FCCI_EINVAL, "q, k_cache and v_cache are required");
+    if (attention && !d->out) return bad(FCCI_EINVAL, "out is required");
+    if ((d->k_new == nullptr) != (d->v_new == nullptr)) return bad(FCCI_EINVAL, "k_new and v_new go together");
+    if (!attention && !d->k_new) return bad(FCCI_EINVAL, "k_new/v_new are required");
+    if (d->capacity <= 0) return bad(FCCI_EINVAL, "capacity must be positive");
+    if (d->rotary_dim < 0 || d->rotary_dim > d->D || (d->rotary_dim & 1))
+        return bad(FCCI_EINVAL, "rotary_dim must be even and within head_dim");
+    if (d->advance && !d->seq_lens) return bad(FCCI_EINVAL, "advance needs seq_lens");
+    if (!d->seq_lens && d->fixed_len < 0) return bad(FCCI_EINVAL, "fixed_len must be non-negative");
     if (attention) {
-        if (!aligned16(d->k_cache) || !aligned16(d->v_cache)) return FCCI_EINVAL;
+        if (!aligned16(d->k_cache) || !aligned16(d->v_cache)) return bad(FCCI_EINVAL, "arena base not 16-byte aligned");
         const int64_t ks[6] = {d->k_stride_t, d->k_stride_h, d->k_stride_b, d->v_stride_t, d->v_stride_h, d->v_stride_b};
         for (int i = 0; i < 6; ++i)
-            if (ks[i] < 0 || (ks[i] & 7)) return FCCI_EINVAL;
-        if (d->k_stride_t == 0 || d->v_stride_t == 0) return FCCI_EINVAL;
-        if ((reinterpret_cast<uintptr_t>(d->out) & 3) || (d->out_stride_h & 1) || (d->out_stride_b & 1)) return FCCI_EINVAL;
+            if (ks[i] < 0 || (ks[i] & 7)) return bad(FCCI_EINVAL, "arena strides must be non-negative multiples of 8");
+        if (d->k_stride_t == 0 || d->v_stride_t == 0) return bad(FCCI_EINVAL, "arena token stride is zero");
+        if ((reinterpret_cast<uintptr_t>(d->out) & 3) || (d->out_stride_h & 1) || (d->out_stride_b & 1))
+            return bad(FCCI_EINVAL, "out must be 4-byte aligned with even strides");
     }
     const int E = d->D / 32;
     if (d->k_new) {
@@ -940,7 +947,7 @@ static int fill_params(const fcci_decode_desc* d, Params& p, bool attention) {
         if (((uintptr_t)d->k_cache & a) || ((uintptr_t)d->v_cache & a) || (d->k_stride_t * 2 & (int64_t)a) ||
             (d->k_stride_h * 2 & (int64_t)a) || (d->k_stride_b * 2 & (int64_t)a) || (d->v_stride_t * 2 & (int64_t)a) ||
             (d->v_stride_h * 2 & (int64_t)a) || (d->v_stride_b * 2 & (int64_t)a))
-            return FCCI_EINVAL;
+            return bad(FCCI_EINVAL, "arena rows misaligned for the append");
     }
     memset(&p, 0, sizeof(p));
     p.q = static_cast<const __half*>(d->q);
@@ -993,7 +1000,7 @@ static void bind_workspace(Params& p, void* ws, const WorkspaceLayout& L) {
 int decode_attention(const fcci_decode_desc* d, cudaStream_t stream) {
     Params p;
     int rc = fill_params(d, p, true);
-    if (rc) return set_status(rc, "fcci_decode_attention: invalid descriptor");
+    if (rc) return rc;
     const int G = p.G;
     const int NB = G <= 8 ? 1 : (G <= 16 ? 2 : 0);
     if (NB == 0 || (d->D == 256 && NB == 2))
@@ -1045,7 +1052,7 @@ int decode_attention(const fcci_decode_desc* d, cudaStream_t stream) {
 int rope_append(const fcci_decode_desc* d, cudaStream_t stream) {
     Params p;
     int rc = fill_params(d, p, false);
-    if (rc) return set_status(rc, "fcci_rope_append: invalid descriptor");
+    if (rc) return rc;
     if (d->workspace) {
         int dev = 0;
         cudaGetDevice(&dev);
