@@ -137,3 +137,34 @@ def test_compare_metric():
     a = torch.tensor([1.0, 2.0, 3.0], dtype=torch.float64)
     ma, rel = O.compare(a + 1e-3, a)
     assert abs(ma - 1e-3) < 1e-9 and rel < 1e-3
+
+
+def test_oracle_matches_reference_cuda_kernel_golden():
+    """Outputs of the reference's attn_varlen kernel, built from its sources and run on a
+    B200 (tests/golden/make_golden_gpu.py), against the oracle on the same seeded inputs."""
+    from helpers import sha256_of
+
+    d = golden("ref_kernels.pt")
+    assert len(d["attn_varlen"]) >= 9
+    for c in d["attn_varlen"]:
+        H, T, D, seed = c["H"], c["T"], c["D"], c["seed"]
+        q = randn_half((H, D), 1000 * seed + 1)
+        k = randn_half((H, T, D), 1000 * seed + 2)
+        v = randn_half((H, T, D), 1000 * seed + 3)
+        assert (sha256_of(q), sha256_of(k), sha256_of(v)) == (c["sha_q"], c["sha_k"], c["sha_v"])
+        ma, rel = O.compare(O.attn_varlen_forward(q, k, v, T, c["scale"]), c["ctx"].float())
+        assert ma <= O.MAX_ABS_TOL and rel <= O.REL_L2_TOL, (H, T, D, ma, rel)
+
+
+def test_oracle_placeholder_matches_reference_kernel_golden():
+    from helpers import sha256_of
+
+    d = golden("ref_kernels.pt")
+    for c in d["capture_decode"]:
+        L, H, ml, D, seed = c["L"], c["H"], c["max_len"], c["D"], c["seed"]
+        ak = randn_half((L, 1, H, ml, D), 1000 * seed + 1)
+        av = randn_half((L, 1, H, ml, D), 1000 * seed + 2)
+        nk, nv, lg, nT = O.placeholder_step(c["ctrl"], ak, av, c["T"], c["vocab"])
+        assert sha256_of(nk) == c["sha_k_out"] and sha256_of(nv) == c["sha_v_out"]
+        assert torch.nonzero(lg[0]).flatten().tolist() == c["logits_nonzero"].tolist()
+        assert float(lg.sum()) == c["logits_sum"] and nT == c["seq_len_out"]
