@@ -1,0 +1,75 @@
+// fcci_decode_attention_noalloc: the decode-attention step with its scratch in a
+// fixed device array that this library owns, for callers that cannot allocate
+// device memory themselves.
+//
+// Who needs it: a caller embedded in a host runtime that owns every byte of
+// device memory (a serving framework with its own memory pool, or a plugin
+// whose allocator is not reachable from its language's FFI) may not call
+// cudaMalloc at all, and a caller on a latency-critical path may not afford
+// one (cudaMalloc/cudaFree can synchronize the device). Such a caller still
+// passes its own inputs and outputs; only the split-KV scratch (partial
+// results, merge counters, error word) comes from here.
+#include <cuda_runtime.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "fcci_decode.h"
+#include "fcci_internal.h"
+
+namespace fcci {
+
+// Split-KV scratch of the allocation-free entry point. Every GPU that loads this
+// library holds these FCCI_NOALLOC_SCRATCH_BYTES until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FCCI_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on device `dev` (the current device). In
+// host code the array's name is only a stand-in for the symbol, so the address
+// is looked up once per device with cudaGetSymbolAddress.
+static int noalloc_scratch(int dev, void** out) {
+    static std::once_flag once[128];
+    static void* addr[128];
+    static cudaError_t err[128];
+    if (dev < 0 || dev >= 128) return set_status(FCCI_EINVAL, "fcci_decode_attention_noalloc: device index");
+    std::call_once(once[dev], [dev]() {
+        void* p = nullptr;
+        err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        addr[dev] = p;
+        if (err[dev] != cudaSuccess) cudaGetLastError();
+    });
+    if (err[dev] != cudaSuccess) return set_cuda_status(err[dev]);
+    *out = addr[dev];
+    return FCCI_OK;
+}
+
+}  // namespace fcci
+
+extern "C" int fcci_decode_attention_noalloc(const fcci_decode_desc* desc, cudaStream_t stream) {
+    if (!desc) return fcci::set_status(FCCI_EINVAL, "fcci_decode_attention_noalloc: descriptor is NULL");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fcci::set_cuda_status(e);
+    const size_t need = fcci_decode_workspace_bytes(desc->B, desc->Hq, desc->Hkv, desc->D, dev);
+    if (need == 0) return fcci::set_status(FCCI_EINVAL, "fcci_decode_attention_noalloc: invalid shape");
+    if (need > FCCI_NOALLOC_SCRATCH_BYTES) {
+        static thread_local char msg[200];
+        snprintf(msg, sizeof(msg),
+                 "fcci_decode_attention_noalloc: this shape needs %zu bytes of scratch; the built-in scratch holds %u "
+                 "bytes (use fcci_decode_attention with a caller workspace)",
+                 need, (unsigned)FCCI_NOALLOC_SCRATCH_BYTES);
+        return fcci::set_status(FCCI_EWORKSPACE, msg);
+    }
+    void* scratch = nullptr;
+    int rc = fcci::noalloc_scratch(dev, &scratch);
+    if (rc) return rc;
+    // the array keeps the previous call's contents: the counters and the error
+    // word must start at zero
+    const fcci::WorkspaceLayout L =
+        fcci::workspace_layout(desc->B, desc->Hq, desc->Hkv, desc->D, fcci::max_grid(dev));
+    e = cudaMemsetAsync(scratch, 0, L.zero_bytes, stream);
+    if (e != cudaSuccess) return fcci::set_cuda_status(e);
+    fcci_decode_desc d = *desc;
+    d.workspace = scratch;
+    d.workspace_bytes = FCCI_NOALLOC_SCRATCH_BYTES;
+    return fcci_decode_attention(&d, stream);
+}

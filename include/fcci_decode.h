@@ -132,6 +132,26 @@ typedef struct fcci_decode_desc {
 
 int fcci_decode_attention(const fcci_decode_desc* desc, cudaStream_t stream);
 
+/*
+ * Allocation-free form of fcci_decode_attention. It has no counterpart in the
+ * reference. It is for callers that may not call cudaMalloc: code hosted in a
+ * runtime that owns all device memory (its own pool, or an allocator its FFI
+ * cannot reach), or a latency-critical path that cannot pay for an allocation.
+ * The caller still passes inputs and outputs; desc->workspace and
+ * workspace_bytes are ignored. The split-KV scratch is a fixed array of
+ * FCCI_NOALLOC_SCRATCH_BYTES (8 MiB) inside this library, resident on every GPU
+ * that loads it until the process exits. Shapes needing more scratch than that
+ * (see fcci_decode_workspace_bytes) are rejected with FCCI_EWORKSPACE and a
+ * message. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call before
+ * any stream capture. Each call zeroes the array's counters and error word on
+ * `stream` first. All calls share the one array: calls that overlap on the GPU
+ * (other streams, other threads) race and must be serialised by the caller.
+ * Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+ */
+#define FCCI_NOALLOC_SCRATCH_BYTES (8u << 20)
+int fcci_decode_attention_noalloc(const fcci_decode_desc* desc, cudaStream_t stream);
+
 /* RoPE(q, k_new) at T_b and append of (k_rot, v_new) at T_b; no attention.
  * Same descriptor; out/scale/workspace/split are ignored; q_rot_out receives
  * the rotated query when non-NULL; advance requires no workspace here (the
