@@ -162,7 +162,7 @@ struct Layout {
                sizeof(uint64_t) * 2 * stages + sizeof(int) * 8;
     }
     static __host__ size_t smem_bytes(int stages, int B, bool split) {
-        return 1024 + fixed_bytes(stages) + (split ? sizeof(int) * (B + 1) : 0);
+        return 1024 + fixed_bytes(stages) + (split ? sizeof(int) * (B + 1) + sizeof(int) * 3 * B : 0);
     }
 };
 
@@ -190,7 +190,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     uint64_t* full = reinterpret_cast<uint64_t*>(rope_cs + D / 2);
     uint64_t* empty = full + S;
     int* misc = reinterpret_cast<int*>(empty + S);
-    int* tile_base = misc + 8;
+    int* tile_base = misc + 8;        // [B+1] prefix of tiles per sequence (x Hkv), split mode
+    int* seqT = tile_base + p.B + 1;  // [B] T_b, split mode
+    int* seqL = seqT + p.B;           // [B] keys attended (0 when invalid)
+    int* seqBase = seqL + p.B;        // [B] first arena row of the sequence
     volatile int* abort_flag = misc;
 
     const int tid = threadIdx.x;
@@ -221,6 +224,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         for (int b = lo; b < hi; ++b) {
             const SeqInfo si = seq_info(p, b);
             if (!si.ok && blockIdx.x == 0) set_error(p, FCCI_DEV_ERR_CAPACITY);
+            seqT[b] = si.T;
+            seqL[b] = si.L;
+            seqBase[b] = si.tok_base;
             const int c = tiles_of(si.L) * Hkv;
             tile_base[b + 1] = c;
             local += c;
@@ -286,7 +292,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         if (lane == 0 && ntiles > 0) {
             const uint64_t pol = l2_policy_evict_first();
             int b = b0, h = h0, j = j0;
-            SeqInfo si = seq_info(p, b);
+            SeqInfo si = p.split ? SeqInfo{seqT[b], seqL[b], seqBase[b], true} : seq_info(p, b);
             int tiles = tiles_of(si.L);
             int issued = 0;
             for (int it = 0; it < ntiles; ++it) {
@@ -319,7 +325,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     if (++h == Hkv) {
                         h = 0;
                         if (++b < B) {
-                            si = seq_info(p, b);
+                            si = p.split ? SeqInfo{seqT[b], seqL[b], seqBase[b], true} : seq_info(p, b);
                             tiles = tiles_of(si.L);
                         }
                     }
@@ -348,24 +354,18 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         int cached_pos = -1;
 
         int b = b0, h = h0, j = j0;
-        SeqInfo si = seq_info(p, b);
+        SeqInfo si = p.split ? SeqInfo{seqT[b], seqL[b], seqBase[b], true} : seq_info(p, b);
         int tiles = tiles_of(si.L);
         bool seg_start = true;
 
         for (int it = 0; it < ntiles; ++it) {
             if (seg_start) {
                 seg_start = false;
-                // ---- rotated queries of the group (shared by the 4 warps)
-                if (rot > 0 && si.T != cached_pos) {
-                    for (int i = ctid; i < rhalf; i += kConsumerThreads)
-                        rope_cs[i] = rope_cs_entry(p.rope_theta, i, rhalf, si.T);
-                    cached_pos = si.T;
-                    named_bar_sync(kConsumerBar, kConsumerThreads);
-                }
+                // ---- rotated queries of the group (shared by the 4 warps): issue the
+                //      query loads first (one L2 round trip), then the RoPE table
                 const bool write_qrot = (p.q_rot_out != nullptr) && (j == 0);
                 const __half* qb = p.q + (int64_t)b * p.q_sb;
-                // all loads first (one L2 round trip), then rotate; element e -> (head, dim)
-                constexpr int NQ = G8 * D / kConsumerThreads;
+                constexpr int NQ = G8 * D / kConsumerThreads;  // element e -> (head, dim)
                 __half qx[NQ], qp[NQ];
 #pragma unroll
                 for (int k = 0; k < NQ; ++k) {
@@ -378,6 +378,12 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                         qx[k] = qr[d];
                         if (d < rot) qp[k] = qr[d < rhalf ? d + rhalf : d - rhalf];
                     }
+                }
+                if (rot > 0 && si.T != cached_pos) {
+                    for (int i = ctid; i < rhalf; i += kConsumerThreads)
+                        rope_cs[i] = rope_cs_entry(p.rope_theta, i, rhalf, si.T);
+                    cached_pos = si.T;
+                    named_bar_sync(kConsumerBar, kConsumerThreads);
                 }
 #pragma unroll
                 for (int k = 0; k < NQ; ++k) {
@@ -659,30 +665,45 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                         }
                         named_bar_sync(kConsumerBar, kConsumerThreads);
                         const float* po = p.part_o + (size_t)(pidx + c0) * G * D;
-                        for (int e = ctid * 2; e < G * D; e += 2 * kConsumerThreads) {
-                            const int hh = e / D;
-                            float o0 = 0.f, o1 = 0.f;
-                            int c = 0;
-                            for (; c + 4 <= nparts; c += 4) {
-                                float2 v[4];
+                        // every element of this thread for up to 8 pieces per batch: one
+                        // L2 round trip per 8 pieces instead of one per element and piece
+                        constexpr int NE = G8 * D / (2 * kConsumerThreads);  // float2 per thread
+                        constexpr int PB = NE >= 16 ? 1 : 16 / NE;  // pieces per batch: <= 16 loads in flight
+                        float2 o[NE];
 #pragma unroll
-                                for (int u = 0; u < 4; ++u)
-                                    v[u] = __ldcg(reinterpret_cast<const float2*>(po + (size_t)(c + u) * G * D + e));
+                        for (int k = 0; k < NE; ++k) o[k] = make_float2(0.f, 0.f);
+                        for (int c = 0; c < nparts; c += PB) {
+                            float2 v[PB][NE];
 #pragma unroll
-                                for (int u = 0; u < 4; ++u) {
-                                    const float w = wts[(c + u) * G + hh];
-                                    o0 += w * v[u].x;
-                                    o1 += w * v[u].y;
+                            for (int u = 0; u < PB; ++u)
+#pragma unroll
+                                for (int k = 0; k < NE; ++k) {
+                                    const int e = 2 * (ctid + k * kConsumerThreads);
+                                    v[u][k] = (c + u < nparts && e < G * D)
+                                                  ? __ldcg(reinterpret_cast<const float2*>(po + (size_t)(c + u) * G * D + e))
+                                                  : make_float2(0.f, 0.f);
                                 }
+#pragma unroll
+                            for (int u = 0; u < PB; ++u)
+#pragma unroll
+                                for (int k = 0; k < NE; ++k) {
+                                    const int e = 2 * (ctid + k * kConsumerThreads);
+                                    if (c + u < nparts && e < G * D) {
+                                        const float w = wts[(c + u) * G + e / D];
+                                        o[k].x += w * v[u][k].x;
+                                        o[k].y += w * v[u][k].y;
+                                    }
+                                }
+                        }
+#pragma unroll
+                        for (int k = 0; k < NE; ++k) {
+                            const int e = 2 * (ctid + k * kConsumerThreads);
+                            if (e < G * D) {
+                                const int hh = e / D;
+                                const int d = e - hh * D;
+                                *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) =
+                                    __floats2half2_rn(o[k].x, o[k].y);
                             }
-                            for (; c < nparts; ++c) {
-                                const float2 v = __ldcg(reinterpret_cast<const float2*>(po + (size_t)c * G * D + e));
-                                const float w = wts[c * G + hh];
-                                o0 += w * v.x;
-                                o1 += w * v.y;
-                            }
-                            const int d = e - hh * D;
-                            *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) = __floats2half2_rn(o0, o1);
                         }
                         named_bar_sync(kConsumerBar, kConsumerThreads);
                         if (ctid == 0) atomicExch(&p.pair_cnt[pidx], 0u);
@@ -696,7 +717,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 if (++h == Hkv) {
                     h = 0;
                     if (++b < B) {
-                        si = seq_info(p, b);
+                        si = p.split ? SeqInfo{seqT[b], seqL[b], seqBase[b], true} : seq_info(p, b);
                         tiles = tiles_of(si.L);
                     }
                 }
