@@ -130,10 +130,14 @@ __device__ __forceinline__ int cta_of_tile(long long t, long long N, long long C
 // Accurate RoPE table entry i for position pos: the reference computes
 // inv = theta ** (-i / half) and angle = pos * inv in fp32, then cos/sin in fp32
 // (scripts/direct_custom_decode_500.py:96-100).
-__device__ __forceinline__ float2 rope_cs_entry(float theta, int i, int half, int pos) {
+__device__ __forceinline__ float rope_angle(float theta, int i, int half, int pos) {
     const float e = __fdiv_rn(-(float)i, (float)half);
     const float inv = powf(theta, e);
-    const float ang = __fmul_rn((float)pos, inv);
+    return __fmul_rn((float)pos, inv);
+}
+
+__device__ __forceinline__ float2 rope_cs_entry(float theta, int i, int half, int pos) {
+    const float ang = rope_angle(theta, i, half, pos);
     return make_float2(cosf(ang), sinf(ang));
 }
 
@@ -231,19 +235,19 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
             tile_base[b + 1] = c;
             local += c;
         }
-        scratch[tid] = local;
-        __syncthreads();
-        if (tid == 0) {
-            int run = 0;
-            for (int i = 0; i < kThreads; ++i) {
-                const int v = scratch[i];
-                scratch[i] = run;
-                run += v;
-            }
-            tile_base[0] = 0;
+        // exclusive prefix of the per-thread sums: shuffle scan per warp, then the
+        // 5 warp totals
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
         }
+        if (lane == 31) scratch[warp] = incl;
+        if (tid == 0) tile_base[0] = 0;
         __syncthreads();
-        int run = scratch[tid];
+        int run = incl - local;
+        for (int w = 0; w < warp; ++w) run += scratch[w];
         for (int b = lo; b < hi; ++b) {
             run += tile_base[b + 1];
             tile_base[b + 1] = run;
@@ -380,8 +384,12 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     }
                 }
                 if (rot > 0 && si.T != cached_pos) {
-                    for (int i = ctid; i < rhalf; i += kConsumerThreads)
-                        rope_cs[i] = rope_cs_entry(p.rope_theta, i, rhalf, si.T);
+                    for (int i = ctid; i < 2 * rhalf; i += kConsumerThreads) {
+                        const int k = i < rhalf ? i : i - rhalf;
+                        const float ang = rope_angle(p.rope_theta, k, rhalf, si.T);
+                        if (i < rhalf) rope_cs[k].x = cosf(ang);
+                        else rope_cs[k].y = sinf(ang);
+                    }
                     cached_pos = si.T;
                     named_bar_sync(kConsumerBar, kConsumerThreads);
                 }
@@ -633,65 +641,58 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 }
                 named_bar_sync(kConsumerBar, kConsumerThreads);
                 if (!whole) {
-                    // ---- the last piece of a cut pair merges every piece's (o, lse)
-                    __threadfence();
-                    named_bar_sync(kConsumerBar, kConsumerThreads);
+                    // ---- the last piece of a cut pair merges every piece's (o, lse).
+                    //      The barrier above orders this CTA's piece stores before thread
+                    //      0's fence and counter increment (release); the last arriver
+                    //      fences again (acquire) before anyone reads the pieces.
                     if (ctid == 0) {
+                        __threadfence();
                         const unsigned old = atomicAdd(&p.pair_cnt[pidx], 1u);
                         misc[1] = (old == (unsigned)(c1 - c0)) ? 1 : 0;
+                        if (misc[1]) __threadfence();
                     }
                     named_bar_sync(kConsumerBar, kConsumerThreads);
                     if (misc[1]) {
-                        // merge the pieces: lse of every piece into shared memory (parallel
-                        // loads), per-head weights, then the weighted sum of the partial o's
-                        // with several pieces' loads in flight per thread
-                        __threadfence();
+                        // each thread merges its own elements over all pieces with a running
+                        // log-sum-exp; loads of PB pieces are in flight at once
                         const int nparts = c1 - c0 + 1;
-                        float* wts = red_acc;  // [nparts][G]; free after the segment merge above
-                        for (int idx = ctid; idx < nparts * G; idx += kConsumerThreads)
-                            wts[idx] = __ldcg(p.part_lse + (size_t)(pidx + c0) * G + idx);
-                        named_bar_sync(kConsumerBar, kConsumerThreads);
-                        for (int hh = ctid; hh < G; hh += kConsumerThreads) {
-                            float LSE = -INFINITY;
-                            for (int c = 0; c < nparts; ++c) LSE = fmaxf(LSE, wts[c * G + hh]);
-                            float W = 0.f;
-                            for (int c = 0; c < nparts; ++c) {
-                                const float w = LSE == -INFINITY ? 0.f : ex2(wts[c * G + hh] - LSE);
-                                wts[c * G + hh] = w;
-                                W += w;
-                            }
-                            const float inv = W > 0.f ? 1.f / W : 0.f;
-                            for (int c = 0; c < nparts; ++c) wts[c * G + hh] *= inv;
-                        }
-                        named_bar_sync(kConsumerBar, kConsumerThreads);
+                        const float* pl = p.part_lse + (size_t)(pidx + c0) * G;
                         const float* po = p.part_o + (size_t)(pidx + c0) * G * D;
-                        // every element of this thread for up to 8 pieces per batch: one
-                        // L2 round trip per 8 pieces instead of one per element and piece
                         constexpr int NE = G8 * D / (2 * kConsumerThreads);  // float2 per thread
-                        constexpr int PB = NE >= 16 ? 1 : 16 / NE;  // pieces per batch: <= 16 loads in flight
-                        float2 o[NE];
+                        constexpr int PB = NE >= 8 ? 2 : 16 / (2 * NE);     // pieces per batch
+                        float Mx[NE], Wt[NE];
+                        float2 Ov[NE];
 #pragma unroll
-                        for (int k = 0; k < NE; ++k) o[k] = make_float2(0.f, 0.f);
+                        for (int k = 0; k < NE; ++k) {
+                            Mx[k] = -INFINITY;
+                            Wt[k] = 0.f;
+                            Ov[k] = make_float2(0.f, 0.f);
+                        }
                         for (int c = 0; c < nparts; c += PB) {
-                            float2 v[PB][NE];
+                            float lv[PB][NE];
+                            float2 ov[PB][NE];
 #pragma unroll
                             for (int u = 0; u < PB; ++u)
 #pragma unroll
                                 for (int k = 0; k < NE; ++k) {
                                     const int e = 2 * (ctid + k * kConsumerThreads);
-                                    v[u][k] = (c + u < nparts && e < G * D)
-                                                  ? __ldcg(reinterpret_cast<const float2*>(po + (size_t)(c + u) * G * D + e))
+                                    const bool ok = c + u < nparts && e < G * D;
+                                    lv[u][k] = ok ? __ldcg(pl + (size_t)(c + u) * G + e / D) : -INFINITY;
+                                    ov[u][k] = ok ? __ldcg(reinterpret_cast<const float2*>(po + (size_t)(c + u) * G * D + e))
                                                   : make_float2(0.f, 0.f);
                                 }
 #pragma unroll
                             for (int u = 0; u < PB; ++u)
 #pragma unroll
                                 for (int k = 0; k < NE; ++k) {
-                                    const int e = 2 * (ctid + k * kConsumerThreads);
-                                    if (c + u < nparts && e < G * D) {
-                                        const float w = wts[(c + u) * G + e / D];
-                                        o[k].x += w * v[u][k].x;
-                                        o[k].y += w * v[u][k].y;
+                                    const float lse = lv[u][k];
+                                    if (lse != -INFINITY) {
+                                        const float mn = fmaxf(Mx[k], lse);
+                                        const float a = ex2(Mx[k] - mn), w = ex2(lse - mn);
+                                        Wt[k] = Wt[k] * a + w;
+                                        Ov[k].x = Ov[k].x * a + w * ov[u][k].x;
+                                        Ov[k].y = Ov[k].y * a + w * ov[u][k].y;
+                                        Mx[k] = mn;
                                     }
                                 }
                         }
@@ -701,11 +702,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                             if (e < G * D) {
                                 const int hh = e / D;
                                 const int d = e - hh * D;
+                                const float inv = Wt[k] > 0.f ? 1.f / Wt[k] : 0.f;
                                 *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) =
-                                    __floats2half2_rn(o[k].x, o[k].y);
+                                    __floats2half2_rn(Ov[k].x * inv, Ov[k].y * inv);
                             }
                         }
-                        named_bar_sync(kConsumerBar, kConsumerThreads);
                         if (ctid == 0) atomicExch(&p.pair_cnt[pidx], 0u);
                     }
                 }
