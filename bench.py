@@ -140,17 +140,29 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic(workload_name: str):
-    """DRAM bytes per launch of the decode kernel from the committed ncu summary, if any."""
+def profile_traffic(workload_name: str, alg_bytes: int):
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary, if any.
+
+    The summary records the traffic and the algorithmic bytes of the launch it
+    captured (the whole workload on one GPU). A shard of that workload on N GPUs
+    reads a part of the same arena in proportion to its keys, so the captured
+    traffic is scaled by alg_bytes / captured algorithmic bytes."""
     path = os.path.join(ROOT, "profiles", f"decode_attn_{workload_name}.md")
+    vals = {}
     try:
         with open(path) as f:
             for line in f:
-                if line.strip().startswith("traffic_bytes_per_launch:"):
-                    return int(float(line.split(":", 1)[1].strip()))
+                key, _, val = line.strip().partition(":")
+                if key in ("traffic_bytes_per_launch", "algorithmic_bytes_per_launch") and val.strip():
+                    vals[key] = float(val.strip())
     except OSError:
-        pass
-    return None
+        return None
+    if "traffic_bytes_per_launch" not in vals:
+        return None
+    traffic = vals["traffic_bytes_per_launch"]
+    if vals.get("algorithmic_bytes_per_launch"):
+        traffic *= alg_bytes / vals["algorithmic_bytes_per_launch"]
+    return int(traffic)
 
 
 # ---------------------------------------------------------------- distributed
@@ -321,7 +333,7 @@ def ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    traffic = profile_traffic(w["name"])
+    traffic = profile_traffic(w["name"], per_launch_alg)
     line = {
         "metric": METRIC,
         "value": round(value, 1),
