@@ -27,8 +27,8 @@ NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 LIB = os.path.join(PKG, "libfcci_decode.so")
-LIB_SOURCES = ["decode_attn.cu", "capi.cu", "compat.cu", "noalloc.cu"]
-LIB_HEADERS = ["ptx.cuh", "fcci_internal.h"]
+LIB_SOURCES = ["decode_attn.cu", "capi.cu", "compat.cu", "noalloc.cu", "prefill_attn.cu"]
+LIB_HEADERS = ["ptx.cuh", "tcgen05.cuh", "fcci_internal.h"]
 MODULES = {
     "attn_varlen": "attn_varlen_module.cpp",
     "capture_decode_step": "capture_decode_step_module.cpp",
@@ -56,7 +56,7 @@ def _run(cmd: list[str], cwd: str | None = None) -> None:
 
 
 def _common_headers() -> list[str]:
-    return [os.path.join(INCLUDE, h) for h in ("fcci_decode.h", "fcci_compat.h")]
+    return [os.path.join(INCLUDE, h) for h in ("fcci_decode.h", "fcci_compat.h", "fcci_prefill.h")]
 
 
 def build_library(force: bool = False) -> str:

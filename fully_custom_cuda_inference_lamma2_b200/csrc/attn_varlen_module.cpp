@@ -3,6 +3,7 @@
 // points, all launching the sm_100a kernels of libfcci_decode.so on the current
 // CUDA stream.
 #include "binding_common.h"
+#include "fcci_prefill.h"
 
 using namespace fcci_py;
 
@@ -253,6 +254,114 @@ void rope_append(at::Tensor q, at::Tensor k_new, at::Tensor v_new, at::Tensor k_
     check_rc(fcci_rope_append(&d, current_stream()), "attn_varlen.rope_append");
 }
 
+at::Tensor make_prefill_workspace(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t total_q, int64_t max_seqlen_q,
+                                  int64_t capacity, int64_t rotary_dim, const at::Device& dev) {
+    const size_t bytes = fcci_prefill_workspace_bytes((int32_t)B, (int32_t)Hq, (int32_t)Hkv, (int32_t)D,
+                                                      (int32_t)total_q, (int32_t)max_seqlen_q, (int32_t)capacity,
+                                                      (int32_t)rotary_dim);
+    TORCH_CHECK(bytes > 0, "fcci_prefill_workspace_bytes: invalid shape");
+    at::Tensor ws = at::empty({(int64_t)bytes}, at::TensorOptions().dtype(at::kByte).device(dev));
+    check_rc(fcci_prefill_workspace_init(ws.data_ptr(), bytes, current_stream()), "fcci_prefill_workspace_init");
+    return ws;
+}
+
+// Causal varlen prefill: RoPE(q, k_new) at T_b + i, append into the arena, causal
+// attention of the new tokens over all T_b + n_b keys (tcgen05 tensor cores).
+void prefill_varlen(at::Tensor q, at::Tensor k_new, at::Tensor v_new, at::Tensor k_cache, at::Tensor v_cache,
+                    at::Tensor out, at::Tensor cu_seqlens_q, int64_t max_seqlen_q, c10::optional<at::Tensor> seq_lens,
+                    c10::optional<at::Tensor> cu_seqlens_kv, int64_t fixed_len, double scale, double rope_theta,
+                    int64_t rotary_dim, bool advance, c10::optional<at::Tensor> workspace) {
+    for (auto* t : {&q, &k_new, &v_new, &k_cache, &v_cache, &out}) check_half_cuda(*t, "prefill tensor");
+    check_int32_cuda(cu_seqlens_q, "cu_seqlens_q");
+    TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1, "q must be [total, Hq, D] with a contiguous last dimension");
+    const int64_t total = q.size(0), Hq = q.size(1), D = q.size(2);
+    const int64_t B = cu_seqlens_q.numel() - 1;
+    TORCH_CHECK(B >= 1, "cu_seqlens_q must have B+1 >= 2 entries");
+    TORCH_CHECK(k_new.dim() == 3 && k_new.size(0) == total && k_new.size(2) == D && k_new.stride(2) == 1,
+                "k_new must be [total, Hkv, D]");
+    const int64_t Hkv = k_new.size(1);
+    TORCH_CHECK(v_new.sizes() == k_new.sizes() && v_new.stride(2) == 1, "v_new must be [total, Hkv, D]");
+    TORCH_CHECK(out.sizes() == q.sizes() && out.stride(2) == 1, "out must be [total, Hq, D]");
+    TORCH_CHECK(Hkv > 0 && Hq % Hkv == 0, "Hq must be a multiple of Hkv");
+    const bool packed = cu_seqlens_kv.has_value() && cu_seqlens_kv->defined();
+    int64_t cap;
+    if (packed) {
+        TORCH_CHECK(k_cache.dim() == 3 && k_cache.size(0) == Hkv, "packed arena must be [Hkv, total_tokens, D]");
+        check_int32_cuda(*cu_seqlens_kv, "cu_seqlens_kv");
+        TORCH_CHECK(cu_seqlens_kv->numel() == B + 1, "cu_seqlens_kv must have B+1 entries");
+        cap = k_cache.size(1);
+    } else {
+        TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(0) == B && k_cache.size(1) == Hkv,
+                    "arena must be [B, Hkv, capacity, D]");
+        cap = k_cache.size(2);
+    }
+    TORCH_CHECK(v_cache.sizes() == k_cache.sizes() && k_cache.size(-1) == D, "arena shapes differ");
+    TORCH_CHECK(tma_compatible(k_cache) && tma_compatible(v_cache),
+                "arena must have a contiguous head_dim, 16-byte aligned base and strides");
+    TORCH_CHECK(cap < (int64_t)1 << 31 && total < (int64_t)1 << 31, "sizes exceed int32");
+    c10::cuda::CUDAGuard guard(q.device());
+    fcci_prefill_desc d;
+    std::memset(&d, 0, sizeof(d));
+    d.abi_version = FCCI_PREFILL_ABI_VERSION;
+    d.B = (int32_t)B;
+    d.Hq = (int32_t)Hq;
+    d.Hkv = (int32_t)Hkv;
+    d.D = (int32_t)D;
+    d.total_q = (int32_t)total;
+    d.max_seqlen_q = (int32_t)max_seqlen_q;
+    d.cu_seqlens_q = cu_seqlens_q.data_ptr<int32_t>();
+    d.q = q.data_ptr();
+    d.q_stride_t = q.stride(0);
+    d.q_stride_h = q.stride(1);
+    d.k_new = k_new.data_ptr();
+    d.k_new_stride_t = k_new.stride(0);
+    d.k_new_stride_h = k_new.stride(1);
+    d.v_new = v_new.data_ptr();
+    d.v_new_stride_t = v_new.stride(0);
+    d.v_new_stride_h = v_new.stride(1);
+    d.k_cache = k_cache.data_ptr();
+    d.v_cache = v_cache.data_ptr();
+    if (packed) {
+        d.k_stride_h = k_cache.stride(0);
+        d.k_stride_t = k_cache.stride(1);
+        d.v_stride_h = v_cache.stride(0);
+        d.v_stride_t = v_cache.stride(1);
+        d.cu_seqlens_kv = cu_seqlens_kv->data_ptr<int32_t>();
+    } else {
+        d.k_stride_b = k_cache.stride(0);
+        d.k_stride_h = k_cache.stride(1);
+        d.k_stride_t = k_cache.stride(2);
+        d.v_stride_b = v_cache.stride(0);
+        d.v_stride_h = v_cache.stride(1);
+        d.v_stride_t = v_cache.stride(2);
+    }
+    d.capacity = (int32_t)cap;
+    if (seq_lens.has_value() && seq_lens->defined()) {
+        check_int32_cuda(*seq_lens, "seq_lens");
+        TORCH_CHECK(seq_lens->numel() == B, "seq_lens must have B entries");
+        d.seq_lens = seq_lens->data_ptr<int32_t>();
+    } else {
+        TORCH_CHECK(fixed_len >= 0, "give seq_lens or a non-negative fixed_len");
+        TORCH_CHECK(!advance, "advance needs seq_lens");
+        d.fixed_len = (int32_t)fixed_len;
+    }
+    d.out = out.data_ptr();
+    d.out_stride_t = out.stride(0);
+    d.out_stride_h = out.stride(1);
+    d.scale = scale > 0 ? (float)scale : (float)(1.0 / std::sqrt((double)D));
+    d.rope_theta = (float)rope_theta;
+    d.rotary_dim = (int32_t)(rotary_dim < 0 ? D : rotary_dim);
+    d.advance = advance ? 1 : 0;
+    at::Tensor ws;
+    if (workspace.has_value() && workspace->defined()) ws = *workspace;
+    else ws = make_prefill_workspace(B, Hq, Hkv, D, total, max_seqlen_q, cap, d.rotary_dim, q.device());
+    TORCH_CHECK(ws.is_cuda() && ws.scalar_type() == at::kByte && ws.is_contiguous(),
+                "workspace must be a contiguous uint8 CUDA tensor from make_prefill_workspace()");
+    d.workspace = ws.data_ptr();
+    d.workspace_bytes = (size_t)ws.numel();
+    check_rc(fcci_prefill_attention(&d, current_stream()), "attn_varlen.prefill_varlen");
+}
+
 int64_t read_error(at::Tensor workspace, bool clear) {
     TORCH_CHECK(workspace.is_cuda() && workspace.scalar_type() == at::kByte, "workspace must be a uint8 CUDA tensor");
     c10::cuda::CUDAGuard guard(workspace.device());
@@ -299,6 +408,36 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("Hkv"), py::arg("D"), py::arg("device") = py::none());
     m.def("read_error", &read_error, "Device error word of a workspace (synchronises)", py::arg("workspace"),
           py::arg("clear") = true);
+    m.def("prefill_varlen", &prefill_varlen,
+          "Causal varlen prefill: RoPE(q,k_new) at T_b+i, append into the arena, causal attention over T_b+n_b keys",
+          py::arg("q"), py::arg("k_new"), py::arg("v_new"), py::arg("k_cache"), py::arg("v_cache"), py::arg("out"),
+          py::arg("cu_seqlens_q"), py::arg("max_seqlen_q"), py::arg("seq_lens") = py::none(),
+          py::arg("cu_seqlens_kv") = py::none(), py::arg("fixed_len") = -1, py::arg("scale") = -1.0,
+          py::arg("rope_theta") = 10000.0, py::arg("rotary_dim") = -1, py::arg("advance") = false,
+          py::arg("workspace") = py::none());
+    m.def(
+        "make_prefill_workspace",
+        [](int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t total_q, int64_t max_seqlen_q, int64_t capacity,
+           int64_t rotary_dim, c10::optional<at::Device> device) {
+            at::Device dev = device.has_value() ? *device : at::Device(at::kCUDA, c10::cuda::current_device());
+            c10::cuda::CUDAGuard guard(dev);
+            return make_prefill_workspace(B, Hq, Hkv, D, total_q, max_seqlen_q, capacity,
+                                          rotary_dim < 0 ? D : rotary_dim, dev);
+        },
+        "Zeroed workspace for prefill_varlen() (allocate outside graph capture)", py::arg("B"), py::arg("Hq"),
+        py::arg("Hkv"), py::arg("D"), py::arg("total_q"), py::arg("max_seqlen_q"), py::arg("capacity"),
+        py::arg("rotary_dim") = -1, py::arg("device") = py::none());
+    m.def(
+        "prefill_read_error",
+        [](at::Tensor workspace, bool clear) {
+            TORCH_CHECK(workspace.is_cuda() && workspace.scalar_type() == at::kByte, "workspace must be uint8 CUDA");
+            c10::cuda::CUDAGuard guard(workspace.device());
+            uint32_t flags = 0;
+            check_rc(fcci_prefill_read_error(workspace.data_ptr(), &flags, clear ? 1 : 0, current_stream()),
+                     "attn_varlen.prefill_read_error");
+            return (int64_t)flags;
+        },
+        py::arg("workspace"), py::arg("clear") = true);
     m.def("launch_count", []() { return (int64_t)fcci_launch_count(); });
     m.def(
         "set_tuning", [](int64_t stages, int64_t ctas) { check_rc(fcci_decode_set_tuning((int)stages, (int)ctas), "set_tuning"); },

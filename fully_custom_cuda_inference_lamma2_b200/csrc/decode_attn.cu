@@ -843,27 +843,42 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 4-D map (head_dim, token, kv head, sequence) over an fp16 arena; 64 x 16 boxes,
-// 128-byte swizzle. Strides in elements.
-static int encode_kv_map(CUtensorMap* map, const void* base, int D, int64_t tokens, int Hkv, int Bdim, int64_t st,
-                         int64_t sh, int64_t sb) {
+// fp16 tensor map with 128-byte swizzle. dims[0] is the contiguous dimension;
+// stride_bytes[i] is the byte stride of dims[i + 1]. A stride of an extent-1
+// dimension is never used by a load; it is replaced by the packed value so the
+// encoder's alignment checks pass.
+int encode_f16_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const int64_t* stride_bytes,
+                     const uint32_t* box) {
     auto fn = encode_fn();
-    if (!fn) return FCCI_ETMAP;
-    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)tokens, (cuuint64_t)Hkv, (cuuint64_t)Bdim};
-    int64_t sbytes[3] = {st * 2, sh * 2, sb * 2};
-    // a stride of an extent-1 dimension is never used; give it the packed value
+    if (!fn || rank < 1 || rank > 5) return FCCI_ETMAP;
+    cuuint64_t d[5], st[4];
+    cuuint32_t bx[5], estr[5];
     int64_t prev = 2;  // bytes per element: the stride of dimension 0
-    for (int i = 0; i < 3; ++i) {
-        if (dims[i + 1] == 1) sbytes[i] = ((prev * (int64_t)dims[i] + 15) / 16) * 16;
-        prev = sbytes[i];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = (cuuint64_t)dims[i];
+        bx[i] = box[i];
+        estr[i] = 1;
+        if (i > 0) {
+            int64_t sb = stride_bytes[i - 1];
+            if (dims[i] == 1) sb = ((prev * (int64_t)dims[i - 1] + 15) / 16) * 16;
+            st[i - 1] = (cuuint64_t)sb;
+            prev = sb;
+        }
     }
-    cuuint64_t strides[3] = {(cuuint64_t)sbytes[0], (cuuint64_t)sbytes[1], (cuuint64_t)sbytes[2]};
-    cuuint32_t box[4] = {64, (cuuint32_t)kGroupKeys, 1, 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), d, st, bx, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? FCCI_OK : FCCI_ETMAP;
+}
+
+// 4-D map (head_dim, token, kv head, sequence) over an fp16 arena; 64 x 16 boxes.
+// Strides in elements.
+static int encode_kv_map(CUtensorMap* map, const void* base, int D, int64_t tokens, int Hkv, int Bdim, int64_t st,
+                         int64_t sh, int64_t sb) {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)tokens, (uint64_t)Hkv, (uint64_t)Bdim};
+    const int64_t sbytes[3] = {st * 2, sh * 2, sb * 2};
+    const uint32_t box[4] = {64, (uint32_t)kGroupKeys, 1, 1};
+    return encode_f16_sw128(map, base, 4, dims, sbytes, box);
 }
 
 WorkspaceLayout workspace_layout(int B, int Hq, int Hkv, int D, int grid) {

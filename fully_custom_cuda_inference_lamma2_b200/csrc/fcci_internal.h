@@ -1,5 +1,6 @@
 // Internal declarations shared by the library's translation units.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -25,6 +26,9 @@ int max_grid(int dev);
 int device_sm_count(int dev);
 
 int set_status(int code, const char* msg);
+// fp16 TMA descriptor with 128-byte swizzle (dims[0] contiguous, byte strides of dims[1..]).
+int encode_f16_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const int64_t* stride_bytes,
+                     const uint32_t* box);
 int set_cuda_status(cudaError_t e);
 void count_launch();
 

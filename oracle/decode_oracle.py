@@ -19,6 +19,10 @@ step (paths inside divakar-yadav/Fully_Custom_Cuda_Inference_Lamma2):
   attn_varlen_forward custom_kernels/attn_varlen.cpp:16-45 (attention over the first
                       seq_len keys)
   placeholder_step    custom_kernels/capture_decode_step_kernel.cu:58-92
+  prefill_step        case4_graph_generator_server_ipc.py:1241-1262 (kv_init: the model
+                      forward over the prompt - RoPE at positions T_b + i, causal
+                      attention - and the copy of the rotated keys / values into the
+                      arena rows T_b .. T_b + n_b - 1)
 
 Pinned against the reference's own code run here (tests/golden/make_golden.py:
 RoPE of the decode driver and of the server) and against the reference CUDA
@@ -161,6 +165,100 @@ def decode_step(q, k_cache, v_cache, seq_lens, *, k_new=None, v_new=None, cu_seq
         V = _rows(v_cache, b, 0, L, cu_seqlens)
         ctx[b] = attention(qr, K, V, scale)
     return dict(ctx=ctx, q_rot=q_rot, k_cache=k_cache, v_cache=v_cache, seq_lens=new_lens, ok=ok)
+
+
+def rope_positions(x: torch.Tensor, pos: torch.Tensor, rotary_dim: int, theta: float = 10000.0) -> torch.Tensor:
+    """Rotate-half RoPE of x [n, H, D] where row i sits at position pos[i].
+
+    Row by row the same fp32 arithmetic as rope_rotate_half (angle = pos * inv_freq,
+    cos/sin, x1*cos - x2*sin and x2*cos + x1*sin, rounded to x's dtype), evaluated on
+    x's device."""
+    out = x.clone()
+    if rotary_dim <= 0 or x.shape[0] == 0:
+        return out
+    half = rotary_dim // 2
+    angle = pos.to(device=x.device, dtype=torch.float32).view(-1, 1) * inv_freq(rotary_dim, theta, x.device).view(1, -1)
+    cos, sin = torch.cos(angle).unsqueeze(1), torch.sin(angle).unsqueeze(1)
+    x1 = x[:, :, :half].float()
+    x2 = x[:, :, half:rotary_dim].float()
+    out[:, :, :half] = (x1 * cos - x2 * sin).to(x.dtype)
+    out[:, :, half:rotary_dim] = (x2 * cos + x1 * sin).to(x.dtype)
+    return out
+
+
+def causal_attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, T: int, scale: float) -> torch.Tensor:
+    """Causal attention of n new query rows over L = T + n keys, fp32.
+
+    q [n, Hq, D] (new token i at position T + i); K, V [Hkv, L, D]; query head h reads
+    kv head h // G. Key t is visible to row i when t <= T + i (the causal mask of the
+    HF LlamaAttention forward the reference's kv_init runs). Returns fp32 [n, Hq, D]."""
+    n, Hq, D = q.shape
+    Hkv, L, _ = K.shape
+    G = Hq // Hkv
+    qg = q.float().permute(1, 0, 2).reshape(Hkv, G, n, D)
+    scores = torch.einsum("kgnd,ktd->kgnt", qg, K.float()) * scale
+    rows = torch.arange(n).view(n, 1) + T
+    cols = torch.arange(L).view(1, L)
+    scores = scores.masked_fill(cols > rows, float("-inf"))
+    probs = torch.softmax(scores, dim=-1)
+    out = torch.einsum("kgnt,ktd->kgnd", probs, V.float())
+    return out.reshape(Hq, n, D).permute(1, 0, 2).contiguous()
+
+
+def prefill_step(q, k_new, v_new, k_cache, v_cache, cu_seqlens_q, seq_lens, *, cu_seqlens_kv=None, scale=None,
+                 theta: float = 10000.0, rotary_dim: Optional[int] = None, inplace: bool = False):
+    """Causal prefill of the new tokens of B sequences, on copies of the caches.
+
+    Restates the reference's kv_init (case4_graph_generator_server_ipc.py:1241-1262):
+    the model forward over the prompt (rotate-half RoPE at positions T_b + i, causal
+    softmax(q k^T * scale) v) and the copy of the rotated keys and the values into the
+    arena rows T_b .. T_b + n_b - 1, after which the cached length is T_b + n_b.
+
+    q [total, Hq, D], k_new / v_new [total, Hkv, D] fp16; sequence b owns rows
+    cu_seqlens_q[b] .. cu_seqlens_q[b+1]-1. Caches batched [B, Hkv, cap, D] or packed
+    [Hkv, total_kv, D] with cu_seqlens_kv. A sequence whose T_b + n_b exceeds its
+    capacity is skipped (out rows 0, ok False).
+    Returns dict(out fp32 [total, Hq, D], q_rot fp16, k_cache, v_cache, seq_lens, ok)."""
+    total, Hq, D = q.shape
+    B = int(cu_seqlens_q.numel()) - 1
+    if not inplace:
+        k_cache = k_cache.clone()
+        v_cache = v_cache.clone()
+    scale = (1.0 / math.sqrt(D)) if scale is None else scale
+    rot = D if rotary_dim is None else rotary_dim
+    out = torch.zeros(total, Hq, D, dtype=torch.float32)
+    q_rot = q.clone()
+    new_lens = seq_lens.clone()
+    ok = torch.zeros(B, dtype=torch.bool)
+    for b in range(B):
+        r0, r1 = int(cu_seqlens_q[b]), int(cu_seqlens_q[b + 1])
+        n = r1 - r0
+        T = int(seq_lens[b])
+        if cu_seqlens_kv is None:
+            cap = k_cache.shape[2]
+        else:
+            cap = int(cu_seqlens_kv[b + 1]) - int(cu_seqlens_kv[b])
+        if T < 0 or T + n > cap:
+            continue
+        ok[b] = True
+        new_lens[b] = T + n
+        if n == 0:
+            continue
+        pos = torch.arange(T, T + n)
+        qr = rope_positions(q[r0:r1], pos, rot, theta)
+        kr = rope_positions(k_new[r0:r1], pos, rot, theta)
+        q_rot[r0:r1] = qr
+        if cu_seqlens_kv is None:
+            k_cache[b, :, T:T + n] = kr.permute(1, 0, 2)
+            v_cache[b, :, T:T + n] = v_new[r0:r1].permute(1, 0, 2)
+        else:
+            base = int(cu_seqlens_kv[b])
+            k_cache[:, base + T: base + T + n] = kr.permute(1, 0, 2)
+            v_cache[:, base + T: base + T + n] = v_new[r0:r1].permute(1, 0, 2)
+        K = _rows(k_cache, b, 0, T + n, cu_seqlens_kv)
+        V = _rows(v_cache, b, 0, T + n, cu_seqlens_kv)
+        out[r0:r1] = causal_attention(qr, K, V, T, scale)
+    return dict(out=out, q_rot=q_rot, k_cache=k_cache, v_cache=v_cache, seq_lens=new_lens, ok=ok)
 
 
 def placeholder_step(ctrl: int, arena_k, arena_v, T: int, vocab: int):
