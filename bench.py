@@ -17,7 +17,9 @@ all-gather of ctx per layer that an unsharded output projection would need.
 
 Other workloads: `gqa70b_32k` (batch 4 at 32768 keys), `varlen7b` (64 sequences,
 lengths U[128, 8192], 32 heads, packed arena with cu_seqlens), `mha7b` (32 heads,
-one sequence at 512 cached keys) — each with --layers.
+one sequence at 512 cached keys) — each with --layers — and `prefill16`: the causal
+varlen prefill of 16 prompts of seeded lengths U[256, 4096] (32 heads, RoPE, arena
+append, tcgen05 attention), reported in TFLOP/s of causal attention.
 
 `--impl reference` times the reference's own implementation of the path: its
 attn_varlen CUDA kernel (built from the reference sources into oracle/_ref)
@@ -467,6 +469,289 @@ def cpu_baseline(w, budget_s=10.0, seed=7):
             "tokens_per_s": round(nseq * n / dt, 2)}
 
 
+# ---------------------------------------------------------------- prefill (causal varlen, tcgen05)
+
+PREFILL_METRIC = "causal varlen prefill TFLOP/s (RoPE + arena append + attention), fraction of dense fp16 peak"
+
+
+def prefill_workload(name: str, layers: int | None):
+    """prefill16: 16 prompts of seeded lengths U[256, 4096], 32 heads (MHA), head_dim 128."""
+    g = torch.Generator().manual_seed(5)
+    lens = torch.randint(256, 4097, (16,), generator=g).tolist()
+    return dict(name=name, B=16, Hq=32, Hkv=32, D=128, lens=lens, layers=layers or 1)
+
+
+def prefill_flops(Hq, D, lens):
+    """4 * Hq * D per (query, visible key) pair: QK^T and PV, causal (keys <= position)."""
+    return sum(4 * Hq * D * (L * (L + 1) // 2) for L in lens)
+
+
+def tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured (cuBLAS bf16 burst; fp16 runs at the same rate)"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def prefill_state(w, world, rank, seed=99):
+    import fully_custom_cuda_inference_lamma2_b200 as fcci
+    from fully_custom_cuda_inference_lamma2_b200.sharding import partition_by_cost
+
+    seqs = partition_by_cost([L * (L + 1) / 2 for L in w["lens"]], world)[rank]
+    lens = [w["lens"][i] for i in seqs]
+    Hq, Hkv, D, layers = w["Hq"], w["Hkv"], w["D"], w["layers"]
+    total, B = sum(lens), len(lens)
+    cap = (max(lens) + 127) // 128 * 128
+    g = torch.Generator(device="cuda").manual_seed(seed + rank)
+    q = torch.randn(layers, total, Hq, D, generator=g, device="cuda").half()
+    kn = torch.randn(layers, total, Hkv, D, generator=g, device="cuda").half()
+    vn = torch.randn(layers, total, Hkv, D, generator=g, device="cuda").half()
+    kc = torch.empty(layers, B, Hkv, cap, D, dtype=torch.float16, device="cuda")
+    vc = torch.empty_like(kc)
+    out = torch.empty(layers, total, Hq, D, dtype=torch.float16, device="cuda")
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
+    av = fcci.attn_varlen
+    ws = av.make_prefill_workspace(B, Hq, Hkv, D, total, max(lens), cap)
+    return dict(av=av, lens=lens, q=q, kn=kn, vn=vn, kc=kc, vc=vc, out=out, cu=cu, ws=ws, max_q=max(lens),
+                layers=layers, B=B)
+
+
+def prefill_call(st, l, part="all", q=None, kn=None, vn=None, out=None):
+    st["av"].prefill_varlen(st["q"][l] if q is None else q, st["kn"][l] if kn is None else kn,
+                            st["vn"][l] if vn is None else vn, st["kc"][l], st["vc"][l],
+                            st["out"][l] if out is None else out, st["cu"], st["max_q"], fixed_len=0,
+                            workspace=st["ws"], part=part)
+
+
+def prefill_cpu_baseline(w, budget_s=10.0, seed=8):
+    """The torch-eager fp32 oracle's prefill_step on the host cores, on a bounded sample:
+    one prompt of 512 tokens x all heads, repeated for about budget_s."""
+    sys.path.insert(0, ROOT)
+    from oracle import decode_oracle as O
+
+    threads = cpu_threads()
+    Hq, Hkv, D, n = w["Hq"], w["Hkv"], w["D"], 512
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(n, Hq, D, generator=g).half()
+    kn = torch.randn(n, Hkv, D, generator=g).half()
+    vn = torch.randn(n, Hkv, D, generator=g).half()
+    kc = torch.zeros(1, Hkv, n, D, dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    cu, T = torch.tensor([0, n]), torch.tensor([0])
+    O.prefill_step(q, kn, vn, kc, vc, cu, T)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.prefill_step(q, kn, vn, kc, vc, cu, T)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    fl = prefill_flops(Hq, D, [n]) * reps
+    return {"value": round(fl / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"oracle prefill_step (torch fp32 eager) on one {n}-token prompt x {Hq} heads, "
+                      f"{reps} repetitions in {dt:.1f} s"}
+
+
+def prefill_ours(args):
+    world, rank, local = dist_setup(args.gpus)
+    w = prefill_workload(args.workload, args.layers)
+    st = prefill_state(w, world, rank)
+    L = st["layers"]
+    flops_step = prefill_flops(w["Hq"], w["D"], st["lens"]) * L
+    for i in range(args.warmup):
+        for l in range(L):
+            prefill_call(st, l)
+    torch.cuda.synchronize()
+    barrier(world)
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K * L)]
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        for i in range(K):
+            for l in range(L):
+                e = ev[i * L + l]
+                e[0].record()
+                prefill_call(st, l, "prepare")
+                e[1].record()
+                prefill_call(st, l, "attend")
+                e[2].record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = ev[0][0].elapsed_time(ev[-1][2])
+    ms = max_over_ranks(ms_local, world)
+    attn_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / len(ev)
+    prep_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / len(ev)
+    flops_all = flops_step * K
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([float(flops_all)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        flops_all = float(t.item())
+    value = flops_all / (ms / 1e3) / 1e12
+    peak, peak_src = tensor_peak()
+    per_launch = prefill_flops(w["Hq"], w["D"], st["lens"])
+    achieved = per_launch / (attn_ms / 1e3) / 1e12
+    clocks = clk.summary()
+
+    # e2e through the public call with host buffers: per step and layer, the new
+    # tokens' q/k/v go host -> device (pinned), the step runs, out goes device -> host
+    hq, hk, hv = st["q"][0].cpu().pin_memory(), st["kn"][0].cpu().pin_memory(), st["vn"][0].cpu().pin_memory()
+    ho = torch.empty(st["out"][0].shape, dtype=torch.float16).pin_memory()
+    dq, dk, dv, do = st["q"][0], st["kn"][0], st["vn"][0], st["out"][0]
+    e2e_steps = max(3, min(K, 5))
+    for _ in range(2):
+        dq.copy_(hq, non_blocking=True)
+        prefill_call(st, 0, q=dq, kn=dk, vn=dv, out=do)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        for l in range(L):
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            prefill_call(st, 0, q=dq, kn=dk, vn=dv, out=do)
+            ho.copy_(do, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_flops = flops_step * e2e_steps
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([float(e2e_flops)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        e2e_flops = float(t.item())
+    h2d = (hq.numel() + hk.numel() + hv.numel()) * 2 * L
+    d2h = ho.numel() * 2 * L
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = prefill_cpu_baseline(w, budget_s=args.cpu_seconds)
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    tokens = sum(w["lens"])
+    line = {
+        "metric": PREFILL_METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / K, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) fp16 q/k/v; random-init, no checkpoint)",
+        "config": {"workload": w["name"], "batch": w["B"], "q_heads": w["Hq"], "kv_heads": w["Hkv"],
+                   "head_dim": w["D"], "prompt_lens": "seeded U[256,4096]", "tokens": tokens, "layers": L,
+                   "causal": True, "parallelism": f"sequence shards x{world}",
+                   "l2": "no flush: %.2f GB of q/k/v/arena per layer > 126 MB L2" % (
+                       (st["q"][0].numel() * 3 + st["kc"][0].numel() * 2) * 2 / 1e9)},
+        "tokens_per_s": round(tokens * K * L / (ms / 1e3), 1),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": None,
+                     "kernel": "prefill_attn_kernel", "algorithmic_flops_per_launch": per_launch,
+                     "avg_launch_ms": round(attn_ms, 5), "prepare_avg_ms": round(prep_ms, 5)},
+        "e2e": {"value": round(e2e_flops / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 4),
+                "api": "attn_varlen.prefill_varlen per layer, host q/k/v in, host out"},
+        "gpu_launches": K * L * 2,
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def prefill_reference(args):
+    """The reference's prefill of one layer as its kv_init runs it: one HF model forward per
+    prompt (batch 1) - LlamaRotaryEmbedding + apply_rotary_pos_emb in fp16 and the causal
+    SDPA attention it selects (attn_implementation "sdpa") - then the copy of the rotated
+    keys and the values into the arena rows, per prompt, on the GPU."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    try:
+        from transformers import LlamaConfig
+        from transformers.integrations.sdpa_attention import sdpa_attention_forward
+        from transformers.models.llama import modeling_llama as M
+    except Exception as e:  # transformers missing or changed
+        print(json.dumps({"impl": "reference", "unavailable": f"transformers Llama functions: {e}"}), flush=True)
+        return
+    w = prefill_workload(args.workload, args.layers)
+    Hq, Hkv, D, lens = w["Hq"], w["Hkv"], w["D"], w["lens"]
+    cap = (max(lens) + 127) // 128 * 128
+    cfg = LlamaConfig(hidden_size=Hq * D, num_attention_heads=Hq, num_key_value_heads=Hkv, head_dim=D,
+                      max_position_embeddings=cap, rope_theta=10000.0)
+    rope = M.LlamaRotaryEmbedding(cfg).cuda()
+
+    class _Mod(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.num_key_value_groups = Hq // Hkv
+            self.is_causal = True
+            self.training = False
+
+    mod = _Mod()
+    g = torch.Generator(device="cuda").manual_seed(99)
+    qs = [torch.randn(1, Hq, L, D, generator=g, device="cuda").half() for L in lens]
+    ks = [torch.randn(1, Hkv, L, D, generator=g, device="cuda").half() for L in lens]
+    vs = [torch.randn(1, Hkv, L, D, generator=g, device="cuda").half() for L in lens]
+    arena_k = torch.empty(len(lens), Hkv, cap, D, dtype=torch.float16, device="cuda")
+    arena_v = torch.empty_like(arena_k)
+    x = torch.empty(1, 1, Hq * D, dtype=torch.float16, device="cuda")
+
+    def one_step():
+        for b, L in enumerate(lens):
+            pos = torch.arange(L, device="cuda").view(1, -1)
+            cos, sin = rope(x, pos)
+            q, k = M.apply_rotary_pos_emb(qs[b], ks[b], cos, sin)
+            sdpa_attention_forward(mod, q, k, vs[b], None, scaling=D ** -0.5, is_causal=True)
+            arena_k[b, :, :L].copy_(k[0])
+            arena_v[b, :, :L].copy_(vs[b][0])
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        one_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    fl = prefill_flops(Hq, D, lens) * args.steps
+    value = fl / (ms / 1e3) / 1e12
+    cpu = prefill_cpu_baseline(w, budget_s=args.cpu_seconds) if not args.no_cpu_baseline else None
+    line = {"impl": "reference", "metric": PREFILL_METRIC, "value": round(value, 2), "unit": "TFLOP/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded N(0,1) fp16 q/k/v)",
+            "config": {"workload": w["name"], "batch": w["B"], "q_heads": Hq, "kv_heads": Hkv, "head_dim": D,
+                       "prompt_lens": "seeded U[256,4096]", "layers": 1, "causal": True,
+                       "path": "HF LlamaRotaryEmbedding + apply_rotary_pos_emb + sdpa_attention_forward per "
+                               "prompt, arena copy (case4_graph_generator_server_ipc.py:1241-1262)"},
+            "e2e": {"value": round(value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if world > 1:
+        line["note"] = f"rank 0 of {world} ran the single-GPU reference; other ranks idle"
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------- reference arm
 
 def reference(args):
@@ -596,7 +881,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="gqa70b", choices=["gqa70b", "gqa70b_32k", "varlen7b", "mha7b"])
+    ap.add_argument("--workload", default="gqa70b",
+                    choices=["gqa70b", "gqa70b_32k", "varlen7b", "mha7b", "prefill16"])
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--gather-ctx", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -604,7 +890,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.workload == "prefill16":
+        (prefill_reference if args.impl == "reference" else prefill_ours)(args)
+    elif args.impl == "reference":
         reference(args)
     else:
         ours(args)

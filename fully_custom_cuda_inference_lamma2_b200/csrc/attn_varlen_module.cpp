@@ -270,7 +270,8 @@ at::Tensor make_prefill_workspace(int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
 void prefill_varlen(at::Tensor q, at::Tensor k_new, at::Tensor v_new, at::Tensor k_cache, at::Tensor v_cache,
                     at::Tensor out, at::Tensor cu_seqlens_q, int64_t max_seqlen_q, c10::optional<at::Tensor> seq_lens,
                     c10::optional<at::Tensor> cu_seqlens_kv, int64_t fixed_len, double scale, double rope_theta,
-                    int64_t rotary_dim, bool advance, c10::optional<at::Tensor> workspace) {
+                    int64_t rotary_dim, bool advance, c10::optional<at::Tensor> workspace, const std::string& part) {
+    TORCH_CHECK(part == "all" || part == "prepare" || part == "attend", "part must be 'all', 'prepare' or 'attend'");
     for (auto* t : {&q, &k_new, &v_new, &k_cache, &v_cache, &out}) check_half_cuda(*t, "prefill tensor");
     check_int32_cuda(cu_seqlens_q, "cu_seqlens_q");
     TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1, "q must be [total, Hq, D] with a contiguous last dimension");
@@ -359,7 +360,9 @@ void prefill_varlen(at::Tensor q, at::Tensor k_new, at::Tensor v_new, at::Tensor
                 "workspace must be a contiguous uint8 CUDA tensor from make_prefill_workspace()");
     d.workspace = ws.data_ptr();
     d.workspace_bytes = (size_t)ws.numel();
-    check_rc(fcci_prefill_attention(&d, current_stream()), "attn_varlen.prefill_varlen");
+    if (part == "prepare") check_rc(fcci_prefill_prepare(&d, current_stream()), "attn_varlen.prefill_varlen(prepare)");
+    else if (part == "attend") check_rc(fcci_prefill_attend(&d, current_stream()), "attn_varlen.prefill_varlen(attend)");
+    else check_rc(fcci_prefill_attention(&d, current_stream()), "attn_varlen.prefill_varlen");
 }
 
 int64_t read_error(at::Tensor workspace, bool clear) {
@@ -414,7 +417,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("cu_seqlens_q"), py::arg("max_seqlen_q"), py::arg("seq_lens") = py::none(),
           py::arg("cu_seqlens_kv") = py::none(), py::arg("fixed_len") = -1, py::arg("scale") = -1.0,
           py::arg("rope_theta") = 10000.0, py::arg("rotary_dim") = -1, py::arg("advance") = false,
-          py::arg("workspace") = py::none());
+          py::arg("workspace") = py::none(), py::arg("part") = "all");
     m.def(
         "make_prefill_workspace",
         [](int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t total_q, int64_t max_seqlen_q, int64_t capacity,

@@ -897,17 +897,65 @@ static int fill(const fcci_prefill_desc* d, Params& p, WsLayout& L) {
     return FCCI_OK;
 }
 
-int prefill_attention(const fcci_prefill_desc* d, cudaStream_t stream) {
+// Validated launch state shared by the two halves of a step.
+struct Launch {
     Params p;
     WsLayout L;
-    int rc = fill(d, p, L);
-    if (rc) return rc;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_status(cudaGetLastError());
-    const int sms = device_sm_count(dev);
-    if (sms <= 0) return set_status(FCCI_ECUDA, "fcci_prefill_attention: no device");
-    if (d->total_q == 0) return FCCI_OK;
+    int dev, sms;
+};
 
+static int setup(const fcci_prefill_desc* d, Launch& x) {
+    int rc = fill(d, x.p, x.L);
+    if (rc) return rc;
+    if (cudaGetDevice(&x.dev) != cudaSuccess) return set_cuda_status(cudaGetLastError());
+    x.sms = device_sm_count(x.dev);
+    if (x.sms <= 0) return set_status(FCCI_ECUDA, "fcci_prefill_attention: no device");
+    if (x.dev < 0 || x.dev >= 128) return set_status(FCCI_EINVAL, "fcci_prefill_attention: device index");
+    static std::once_flag flags[128];
+    static cudaError_t attr_err[128];
+    const int dev = x.dev;
+    std::call_once(flags[dev], [dev]() {
+        attr_err[dev] =
+            cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::kAlloc);
+        if (attr_err[dev] == cudaSuccess)
+            attr_err[dev] =
+                cudaFuncSetAttribute(prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    });
+    if (attr_err[dev] != cudaSuccess) return set_cuda_status(attr_err[dev]);
+    return FCCI_OK;
+}
+
+// RoPE table check, RoPE + append of the new tokens, work list.
+int prefill_prepare(const fcci_prefill_desc* d, cudaStream_t stream) {
+    Launch x;
+    int rc = setup(d, x);
+    if (rc) return rc;
+    Params& p = x.p;
+    if (p.total_q == 0) return FCCI_OK;
+    const size_t prep_smem = (size_t)(4 * p.B + 1) * sizeof(int);
+    if (prep_smem > 227 * 1024) return set_status(FCCI_EUNSUPPORTED, "fcci_prefill_attention: batch too large");
+    if (p.rotary_dim > 0) {
+        const int64_t entries = (int64_t)p.table_pos * (p.rotary_dim / 2);
+        int grid = (int)((entries + 255) / 256);
+        if (grid > x.sms * 8) grid = x.sms * 8;
+        if (grid < 1) grid = 1;
+        rope_table_kernel<<<grid, 256, 0, stream>>>(p);
+        count_launch();
+    }
+    int grid = x.sms * 8;
+    if (grid > p.total_q) grid = p.total_q;
+    prefill_prep_kernel<<<grid + 1, kPrepThreads, prep_smem, stream>>>(p);
+    count_launch();
+    return set_cuda_status(cudaGetLastError());
+}
+
+// Causal attention over the work list written by prefill_prepare (same descriptor).
+int prefill_attend(const fcci_prefill_desc* d, cudaStream_t stream) {
+    Launch x;
+    int rc = setup(d, x);
+    if (rc) return rc;
+    Params& p = x.p;
+    if (p.total_q == 0) return FCCI_OK;
     // tensor maps: rotated queries [total_q, Hq, D] (workspace) and the arena
     CUtensorMap mq, mk, mv;
     {
@@ -926,42 +974,10 @@ int prefill_attention(const fcci_prefill_desc* d, cudaStream_t stream) {
         if (!rc) rc = encode_f16_sw128(&mv, p.v_cache, 4, dims, sbv, box);
     }
     if (rc) return set_status(rc, "fcci_prefill_attention: cuTensorMapEncodeTiled rejected a layout");
-
-    static std::once_flag flags[128];
-    static cudaError_t attr_err[128];
-    if (dev < 0 || dev >= 128) return set_status(FCCI_EINVAL, "fcci_prefill_attention: device index");
-    std::call_once(flags[dev], [&]() {
-        attr_err[dev] =
-            cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::kAlloc);
-        if (attr_err[dev] == cudaSuccess)
-            attr_err[dev] =
-                cudaFuncSetAttribute(prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    });
-    if (attr_err[dev] != cudaSuccess) return set_cuda_status(attr_err[dev]);
-    const size_t prep_smem = (size_t)(4 * p.B + 1) * sizeof(int);
-    if (prep_smem > 227 * 1024) return set_status(FCCI_EUNSUPPORTED, "fcci_prefill_attention: batch too large");
-
-    if (p.rotary_dim > 0) {
-        const int64_t entries = (int64_t)p.table_pos * (p.rotary_dim / 2);
-        int grid = (int)((entries + 255) / 256);
-        if (grid > sms * 8) grid = sms * 8;
-        if (grid < 1) grid = 1;
-        rope_table_kernel<<<grid, 256, 0, stream>>>(p);
-        count_launch();
-    }
-    {
-        int grid = sms * 8;
-        if (grid > p.total_q) grid = p.total_q;
-        prefill_prep_kernel<<<grid + 1, kPrepThreads, prep_smem, stream>>>(p);
-        count_launch();
-    }
-    {
-        int64_t items = L.max_items;
-        int grid = sms;
-        if (items < grid) grid = (int)(items > 0 ? items : 1);
-        prefill_attn_kernel<<<grid, kThreads, Smem::kAlloc, stream>>>(mq, mk, mv, p);
-        count_launch();
-    }
+    int grid = x.sms;
+    if (x.L.max_items < grid) grid = (int)(x.L.max_items > 0 ? x.L.max_items : 1);
+    prefill_attn_kernel<<<grid, kThreads, Smem::kAlloc, stream>>>(mq, mk, mv, p);
+    count_launch();
     return set_cuda_status(cudaGetLastError());
 }
 
@@ -969,7 +985,16 @@ int prefill_attention(const fcci_prefill_desc* d, cudaStream_t stream) {
 }  // namespace fcci
 
 extern "C" int fcci_prefill_attention(const fcci_prefill_desc* desc, cudaStream_t stream) {
-    return fcci::pf::prefill_attention(desc, stream);
+    int rc = fcci::pf::prefill_prepare(desc, stream);
+    return rc ? rc : fcci::pf::prefill_attend(desc, stream);
+}
+
+extern "C" int fcci_prefill_prepare(const fcci_prefill_desc* desc, cudaStream_t stream) {
+    return fcci::pf::prefill_prepare(desc, stream);
+}
+
+extern "C" int fcci_prefill_attend(const fcci_prefill_desc* desc, cudaStream_t stream) {
+    return fcci::pf::prefill_attend(desc, stream);
 }
 
 extern "C" size_t fcci_prefill_workspace_bytes(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t total_q,

@@ -16,6 +16,7 @@
  *   fcci_prefill_attention        the whole step (two or three kernel launches on
  *                                 `stream`: RoPE table check, RoPE + append + work
  *                                 list, tcgen05 attention)
+ *   fcci_prefill_prepare / fcci_prefill_attend   its two halves
  *   fcci_prefill_workspace_bytes  size of the caller-owned workspace
  *   fcci_prefill_workspace_init   zero a fresh workspace (stream-ordered)
  *
@@ -91,6 +92,13 @@ typedef struct fcci_prefill_desc {
 } fcci_prefill_desc;
 
 int fcci_prefill_attention(const fcci_prefill_desc* desc, cudaStream_t stream);
+
+/* The two halves of fcci_prefill_attention, for callers that schedule them
+ * separately (same descriptor and workspace, prepare first, on one stream or with
+ * the caller's own ordering): prepare = RoPE table check + RoPE/append of the new
+ * tokens + work list; attend = the causal attention kernel. */
+int fcci_prefill_prepare(const fcci_prefill_desc* desc, cudaStream_t stream);
+int fcci_prefill_attend(const fcci_prefill_desc* desc, cudaStream_t stream);
 
 /* Workspace bytes: rotated queries (total_q x Hq x D fp16), the RoPE cos/sin
  * table (capacity x rotary_dim/2 float2, rebuilt on device only when theta,
