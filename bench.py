@@ -525,6 +525,23 @@ def prefill_call(st, l, part="all", q=None, kn=None, vn=None, out=None):
                             workspace=st["ws"], part=part)
 
 
+def prefill_traffic(flops_per_launch: int):
+    """DRAM bytes per attention launch from the committed ncu summary, scaled to this launch's work
+    (a shard on N GPUs re-reads K/V in proportion to its causal flops)."""
+    vals = {}
+    try:
+        with open(os.path.join(ROOT, "profiles", "prefill_attn_prefill16.md")) as f:
+            for line in f:
+                key, _, val = line.strip().partition(":")
+                if key in ("traffic_bytes_per_launch", "algorithmic_flops_per_launch") and val.strip():
+                    vals[key] = float(val.strip())
+    except OSError:
+        return None
+    if "traffic_bytes_per_launch" not in vals or not vals.get("algorithmic_flops_per_launch"):
+        return None
+    return int(vals["traffic_bytes_per_launch"] * flops_per_launch / vals["algorithmic_flops_per_launch"])
+
+
 def prefill_cpu_baseline(w, budget_s=10.0, seed=8):
     """The torch-eager fp32 oracle's prefill_step on the host cores, on a bounded sample:
     one prompt of 512 tokens x all heads, repeated for about budget_s."""
@@ -660,7 +677,8 @@ def prefill_ours(args):
                        (st["q"][0].numel() * 3 + st["kc"][0].numel() * 2) * 2 / 1e9)},
         "tokens_per_s": round(tokens * K * L / (ms / 1e3), 1),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": None,
+                     "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                     "traffic": prefill_traffic(per_launch),
                      "kernel": "prefill_attn_kernel", "algorithmic_flops_per_launch": per_launch,
                      "avg_launch_ms": round(attn_ms, 5), "prepare_avg_ms": round(prep_ms, 5)},
         "e2e": {"value": round(e2e_flops / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
