@@ -19,7 +19,10 @@ Other workloads: `gqa70b_32k` (batch 4 at 32768 keys), `varlen7b` (64 sequences,
 lengths U[128, 8192], 32 heads, packed arena with cu_seqlens), `mha7b` (32 heads,
 one sequence at 512 cached keys) — each with --layers — and `prefill16`: the causal
 varlen prefill of 16 prompts of seeded lengths U[256, 4096] (32 heads, RoPE, arena
-append, tcgen05 attention), reported in TFLOP/s of causal attention.
+append, tcgen05 attention), reported in TFLOP/s of causal attention; `llama7b`: greedy
+decode of a Llama-2-7B-shaped model (random weights, batch 1) with one CUDA graph per
+token, in tokens/s (`--steps 484 --warmup 15` reproduces the 16 -> 516 KV range of the
+reference's 500-token run).
 
 `--impl reference` times the reference's own implementation of the path: its
 attn_varlen CUDA kernel (built from the reference sources into oracle/_ref)
@@ -770,6 +773,144 @@ def prefill_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- Llama-2-7B greedy decode (config 2)
+
+LLAMA_METRIC = "Llama-2-7B-shaped greedy decode tokens/s, batch 1 (fraction of the weight-read HBM bound)"
+
+
+def llama_ours(args):
+    """Prompt of 16 seeded tokens through the prefill path, then `steps` timed greedy tokens, one
+    CUDA-graph replay each (all 32 layers, device-side length). With the warm-up tokens the KV
+    length goes from 16 to 16 + warmup + steps (516 with the defaults)."""
+    world, rank, local = dist_setup(args.gpus)
+    from fully_custom_cuda_inference_lamma2_b200.llama_decode import LLAMA2_7B, GreedyDecoder, LlamaWeights
+
+    s = LLAMA2_7B
+    W, K = args.warmup, args.steps
+    prompt_len = 16
+    new = 1 + W + K
+    w = LlamaWeights(s, seed=11 + rank)
+    dec = GreedyDecoder(w, capacity=prompt_len + new + 8, max_new_tokens=new + 1)
+    prompt = torch.randint(0, s.vocab, (prompt_len,), generator=torch.Generator().manual_seed(12)).cuda()
+    dec.arena.seq_lens.zero_()
+    dec.step_idx.zero_()
+    dec.prefill(prompt)
+    dec.generated[0:1].copy_(dec.token)
+    dec.step_idx.fill_(1)
+    dec.capture()
+    for _ in range(W):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(K):
+            dec.graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    tok_s = K * world / (ms / 1e3)
+    hbm, hbm_src = peaks()
+    step_bytes = s.weight_bytes()
+    achieved = step_bytes / (ms / K / 1e3) / 1e9
+    final_len = int(dec.arena.seq_lens.item())
+    # e2e: the serving loop's host round trip per token (token id in from pinned host memory,
+    # next id back to the host), through the same graph
+    h_in = torch.zeros(1, dtype=torch.int64).pin_memory()
+    h_out = torch.zeros(1, dtype=torch.int64).pin_memory()
+    h_in.copy_(dec.token.cpu())
+    dec.arena.seq_lens.fill_(prompt_len)  # the same KV range again, from the prompt on
+    dec.step_idx.fill_(1)
+    e2e_steps = min(K, 100)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(e2e_steps):
+        dec.token.copy_(h_in, non_blocking=True)
+        dec.graph.replay()
+        h_out.copy_(dec.token, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        h_in.copy_(h_out)
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1), world)
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": LLAMA_METRIC, "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True,
+        "scaling": "weak" if world > 1 else "strong", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (random-init N(0,0.02) weights from a seed, 16 seeded prompt tokens; no checkpoint)",
+        "config": {"workload": "llama7b", "layers": s.layers, "hidden": s.hidden, "heads": s.heads,
+                   "intermediate": s.intermediate, "vocab": s.vocab, "batch": 1, "prompt": prompt_len,
+                   "kv_len": f"{prompt_len + 1 + W} -> {final_len}", "graphs": "one graph for every length",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "no flush: 13.2 GB of weights per step > 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_source": hbm_src, "traffic": None,
+                     "kernel": "whole token step (cuBLAS GEMVs + decode_attn_kernel + RMSNorm/SwiGLU)",
+                     "algorithmic_bytes_per_step": step_bytes, "avg_step_ms": round(ms / K, 5)},
+        "e2e": {"value": round(e2e_steps / (e2e_ms / 1e3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 8, "api": "graph replay per token, token id host->device and back"},
+        "gpu_launches": K * (s.layers * 4 + 1),  # this library's kernels: 2 RMSNorm, decode, SwiGLU per layer; final RMSNorm
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def llama_reference(args):
+    """The reference's decode of config 2 as it publishes it: HF LlamaForCausalLM greedy
+    generation with its KV cache (fp16, sdpa attention), same shapes, random-init weights."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    try:
+        from transformers import LlamaConfig, LlamaForCausalLM
+    except Exception as e:
+        print(json.dumps({"impl": "reference", "unavailable": f"transformers Llama: {e}"}), flush=True)
+        return
+    W, K = args.warmup, args.steps
+    cfg = LlamaConfig(hidden_size=4096, intermediate_size=11008, num_hidden_layers=32, num_attention_heads=32,
+                      num_key_value_heads=32, vocab_size=32000, rms_norm_eps=1e-5, tie_word_embeddings=True,
+                      rope_theta=10000.0, max_position_embeddings=4096)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(13)
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(cfg).half().eval()
+    prompt = torch.randint(0, 32000, (1, 16), generator=torch.Generator().manual_seed(12)).cuda()
+    gen = dict(do_sample=False, eos_token_id=None, pad_token_id=0)
+    with torch.no_grad():
+        model.generate(prompt, max_new_tokens=W, min_new_tokens=W, **gen)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = model.generate(prompt, max_new_tokens=K, min_new_tokens=K, **gen)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    n = out.shape[1] - prompt.shape[1]
+    value = n / (ms / 1e3)
+    print(json.dumps({"impl": "reference", "metric": LLAMA_METRIC, "value": round(value, 2), "unit": "tokens/s",
+                      "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": round(ms / n, 4),
+                      "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+                      "data": "synthetic (random-init weights, seeded prompt)",
+                      "config": {"workload": "llama7b", "batch": 1, "prompt": 16,
+                                 "path": "HF LlamaForCausalLM.generate, greedy, KV cache, sdpa (the reference's "
+                                         "published decode path)"},
+                      "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+
+
 # ---------------------------------------------------------------- reference arm
 
 def reference(args):
@@ -900,7 +1041,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="gqa70b",
-                    choices=["gqa70b", "gqa70b_32k", "varlen7b", "mha7b", "prefill16"])
+                    choices=["gqa70b", "gqa70b_32k", "varlen7b", "mha7b", "prefill16", "llama7b"])
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--gather-ctx", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -908,7 +1049,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.workload == "prefill16":
+    if args.workload == "llama7b":
+        (llama_reference if args.impl == "reference" else llama_ours)(args)
+    elif args.workload == "prefill16":
         (prefill_reference if args.impl == "reference" else prefill_ours)(args)
     elif args.impl == "reference":
         reference(args)

@@ -912,6 +912,30 @@ static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUten
     });
     if (attr_err[dev] != cudaSuccess) return set_cuda_status(attr_err[dev]);
     const size_t smem = LY::smem_bytes(prm.stages, prm.B, prm.split != 0);
+    if (prm.split) {
+        // a persistent grid larger than what fits at once would run in waves: cap it
+        // by the resident CTAs per SM of this instantiation (its registers can allow
+        // fewer than the shared-memory estimate of the launch shape)
+        static std::mutex mu;
+        static size_t occ_smem[128];
+        static int occ_val[128];
+        int occ = 0;
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            if (occ_val[dev] > 0 && occ_smem[dev] == smem) occ = occ_val[dev];
+        }
+        if (occ == 0) {
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_attn_kernel<D, NB>, kThreads, smem) !=
+                cudaSuccess) {
+                cudaGetLastError();
+                occ = 0;
+            }
+            std::lock_guard<std::mutex> lk(mu);
+            occ_smem[dev] = smem;
+            occ_val[dev] = occ;
+        }
+        if (occ >= 1 && grid > device_sm_count(dev) * occ) grid = device_sm_count(dev) * occ;
+    }
     decode_attn_kernel<D, NB><<<grid, kThreads, smem, st>>>(mk, mv, prm);
     count_launch();
     return set_cuda_status(cudaGetLastError());
