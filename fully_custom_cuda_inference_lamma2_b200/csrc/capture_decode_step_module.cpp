@@ -171,6 +171,41 @@ void rmsnorm_ptr(at::Tensor x, uint64_t w_ptr, at::Tensor y, double eps) {
     check_rc(fcci_last_status(), "rmsnorm_ptr");
 }
 
+// out = W . a with a = RMSNorm(x) * rms_w (when rms_w is given) or x; mode "store",
+// "residual" (out += W . a) or "swiglu" (W holds 2N rows: gate then up; out = SiLU(g) * u).
+void gemv_fused(at::Tensor W, at::Tensor x, at::Tensor out, const std::string& mode,
+                c10::optional<at::Tensor> rms_w, double eps) {
+    TORCH_CHECK(W.is_cuda() && x.is_cuda() && out.is_cuda(), "all tensors must be CUDA");
+    TORCH_CHECK(W.scalar_type() == at::kHalf && x.scalar_type() == at::kHalf && out.scalar_type() == at::kHalf,
+                "W, x, out must be fp16");
+    TORCH_CHECK(W.dim() == 2 && W.stride(1) == 1, "W must be a row-major [rows, K] matrix");
+    TORCH_CHECK(x.is_contiguous() && out.is_contiguous(), "x and out must be contiguous");
+    const int m = mode == "store" ? 0 : (mode == "residual" ? 1 : (mode == "swiglu" ? 2 : -1));
+    TORCH_CHECK(m >= 0, "mode must be 'store', 'residual' or 'swiglu'");
+    const int64_t N = out.numel(), K = x.numel();
+    TORCH_CHECK(W.size(1) == K, "W columns must equal x length");
+    TORCH_CHECK(W.size(0) == (m == 2 ? 2 * N : N), "W rows must be out length (2x for swiglu)");
+    TORCH_CHECK(N < (1ll << 31) && K < (1ll << 31), "sizes exceed int32");
+    fcci_gemv_desc d;
+    std::memset(&d, 0, sizeof(d));
+    d.W = W.data_ptr();
+    d.ld_w = W.stride(0);
+    d.N = (int32_t)N;
+    d.K = (int32_t)K;
+    d.x = x.data_ptr();
+    if (rms_w.has_value() && rms_w->defined()) {
+        TORCH_CHECK(rms_w->is_cuda() && rms_w->scalar_type() == at::kHalf && rms_w->numel() == K &&
+                        rms_w->is_contiguous(),
+                    "rms_w must be a contiguous fp16 [K] CUDA tensor");
+        d.rms_w = rms_w->data_ptr();
+    }
+    d.eps = (float)eps;
+    d.out = out.data_ptr();
+    d.mode = m;
+    c10::cuda::CUDAGuard guard(x.device());
+    check_rc(fcci_gemv_fused(&d, current_stream()), "gemv_fused");
+}
+
 void swiglu(at::Tensor gate, at::Tensor up, at::Tensor act) {
     TORCH_CHECK(gate.is_cuda() && up.is_cuda() && act.is_cuda(), "all tensors must be CUDA");
     TORCH_CHECK(gate.scalar_type() == at::kHalf && up.scalar_type() == at::kHalf && act.scalar_type() == at::kHalf,
@@ -240,6 +275,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("rmsnorm", &rmsnorm, "Case4 fused RMSNorm (fp16)");
     m.def("rmsnorm_ptr", &rmsnorm_ptr, "Case4 fused RMSNorm with weight pointer (fp16)");
     m.def("swiglu", &swiglu, "Case4 SwiGLU (fp16)");
+    m.def("gemv_fused", &gemv_fused,
+          "Batch-1 projection out (=|+=) W . a, a = RMSNorm(x) * rms_w or x; mode store/residual/swiglu",
+          py::arg("W"), py::arg("x"), py::arg("out"), py::arg("mode") = "store", py::arg("rms_w") = py::none(),
+          py::arg("eps") = 1e-5);
     m.def("gate_up_gemm", &gate_up_gemm, "Case4 MLP gate/up GEMMs (fp16, fp32 accum)");
     m.def("down_gemm", &down_gemm, "Case4 MLP down GEMM (fp16, fp32 accum)");
     m.def("logits_gemm_vocab", &logits_gemm_vocab, "Case4 logits GEMM to vocab (fp16->fp32)");

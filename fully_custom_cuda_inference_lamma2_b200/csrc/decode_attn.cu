@@ -148,6 +148,9 @@ __device__ __forceinline__ float rope_elem(float x, float partner, float2 cs, bo
                       : __fadd_rn(__fmul_rn(x, cs.x), __fmul_rn(partner, cs.y));
 }
 
+// Below this many tiles per CTA, uniform-length problems get pair-aligned CTA ranges.
+constexpr int kAlignBelow = 4;
+
 // Most CTAs that can hold pieces of one pair: the split grid never exceeds this.
 constexpr int kMaxPieces = 320;
 
@@ -220,6 +223,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
 
     // ---- tile line: per-sequence tile counts and their prefix (split mode)
+    bool uniform = false;
     if (p.split) {
         int* scratch = reinterpret_cast<int*>(red_acc);  // free until the first segment ends
         const int chunk = (B + kThreads - 1) / kThreads;
@@ -234,6 +238,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
             const int c = tiles_of(si.L) * Hkv;
             tile_base[b + 1] = c;
             local += c;
+            if (b == 0) misc[2] = c;  // sequence 0's tile count, for the uniformity test below
         }
         // exclusive prefix of the per-thread sums: shuffle scan per warp, then the
         // 5 warp totals
@@ -252,6 +257,12 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
             run += tile_base[b + 1];
             tile_base[b + 1] = run;
         }
+        // do all sequences have the same tile count? (misc[2] was written before the
+        // barrier above)
+        bool same = true;
+        for (int b = lo; b < hi; ++b)
+            if (tiles_of(seqL[b]) * Hkv != misc[2]) same = false;
+        uniform = __syncthreads_and(same) != 0;
     } else if (tid == 0 && p.err) {
         const SeqInfo si = seq_info(p, blockIdx.x / Hkv);
         if (!si.ok && (blockIdx.x % Hkv) == 0) set_error(p, FCCI_DEV_ERR_CAPACITY);
@@ -265,6 +276,17 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     if (p.split) {
         N = tile_base[B];
         C = N < (long long)gridDim.x ? N : (long long)gridDim.x;
+        // small uniform problems: use C = pairs * k CTAs with k dividing the tiles of a
+        // pair, so that every range lies inside one pair (a range straddling two pairs
+        // pays a second segment set-up and piece store, which dominate short ranges)
+        const long long P = (long long)B * Hkv;
+        if (uniform && N < (long long)kAlignBelow * gridDim.x && P <= (long long)gridDim.x) {
+            const long long tp = N / P;
+            long long k = (long long)gridDim.x / P;
+            if (k > tp) k = tp;
+            while (k > 1 && tp % k) --k;
+            C = P * k;
+        }
         if ((long long)blockIdx.x < C) {
             t_begin = (long long)blockIdx.x * N / C;
             t_end = ((long long)blockIdx.x + 1) * N / C;

@@ -19,9 +19,11 @@ length; a step neither allocates nor synchronises the host. The prompt is filled
 into the arena by the causal varlen prefill (`attn_varlen.prefill_varlen`), whose
 rows are the same the decode step would have appended.
 
-Projections are torch/cuBLAS matrix products (the callers the decode path keeps);
-RMSNorm and SwiGLU are the `capture_decode_step` kernels; all fp16, as the
-reference's fp16 model.
+Projections (default) are this library's fused batch-1 GEMVs
+(`capture_decode_step.gemv_fused`): RMSNorm in the QKV and gate/up prologues, SwiGLU
+in the gate/up epilogue, the residual adds in the O and down epilogues, five
+launches per layer. `projections="cublas"` runs them as torch/cuBLAS products with
+the separate RMSNorm / SwiGLU kernels instead. All fp16, as the reference's model.
 """
 from __future__ import annotations
 
@@ -99,7 +101,10 @@ class LlamaWeights:
 class GreedyDecoder:
     """Batch-1 greedy decoding with a persistent KV arena and one CUDA graph per token step."""
 
-    def __init__(self, weights: LlamaWeights, capacity: int, max_new_tokens: int = 1024):
+    def __init__(self, weights: LlamaWeights, capacity: int, max_new_tokens: int = 1024, projections: str = "fused"):
+        if projections not in ("fused", "cublas"):
+            raise ValueError("projections must be 'fused' or 'cublas'")
+        self.projections = projections
         self.w = weights
         s = self.s = weights.shape
         dev = weights.embed.device
@@ -124,6 +129,8 @@ class GreedyDecoder:
 
     # ------------------------------------------------------------------ one token step
     def _layer(self, l: int):
+        if self.projections == "fused":
+            return self._layer_fused(l)
         s, w = self.s, self.w
         Hq, Hkv, D = s.heads, s.kv_heads, s.head_dim
         capture_decode_step.rmsnorm(self.x, w.rms_in[l], self.h, s.eps)
@@ -142,13 +149,32 @@ class GreedyDecoder:
         torch.mv(w.w_down[l], self.act, out=self.tmp)
         self.x.add_(self.tmp)
 
+    def _layer_fused(self, l: int):
+        """The same layer in five launches: RMSNorm folded into the QKV and gate/up
+        projections, SwiGLU into gate/up, the residual adds into O and down."""
+        s, w = self.s, self.w
+        Hq, Hkv, D = s.heads, s.kv_heads, s.head_dim
+        gemv = capture_decode_step.gemv_fused
+        gemv(w.w_qkv[l], self.x, self.qkv, "store", w.rms_in[l], s.eps)
+        q = self.qkv[: Hq * D].view(1, Hq, D)
+        k = self.qkv[Hq * D: (Hq + Hkv) * D].view(1, Hkv, D)
+        v = self.qkv[(Hq + Hkv) * D:].view(1, Hkv, D)
+        decode_attention(self.arena, l, q, self.ctx.view(1, Hq, D), k_new=k, v_new=v,
+                         advance=(l == s.layers - 1), rope_theta=s.rope_theta)
+        gemv(w.w_o[l], self.ctx, self.x, "residual")
+        gemv(w.w_gu[l], self.x, self.act, "swiglu", w.rms_post[l], s.eps)
+        gemv(w.w_down[l], self.act, self.x, "residual")
+
     def _step(self):
         """Consumes self.token, leaves the argmax token in self.token and in generated[step_idx]."""
         torch.index_select(self.w.embed, 0, self.token, out=self.x.view(1, -1))
         for l in range(self.s.layers):
             self._layer(l)
-        capture_decode_step.rmsnorm(self.x, self.w.rms_final, self.h, self.s.eps)
-        torch.mv(self.w.embed, self.h, out=self.logits)
+        if self.projections == "fused":
+            capture_decode_step.gemv_fused(self.w.embed, self.x, self.logits, "store", self.w.rms_final, self.s.eps)
+        else:
+            capture_decode_step.rmsnorm(self.x, self.w.rms_final, self.h, self.s.eps)
+            torch.mv(self.w.embed, self.h, out=self.logits)
         torch.argmax(self.logits.view(1, -1), dim=1, out=self.token)
         # the record of generated tokens wraps around: replays beyond max_new_tokens
         # overwrite the oldest entries instead of indexing past the buffer

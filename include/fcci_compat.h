@@ -47,6 +47,31 @@ void swiglu_host(const void* gate, const void* up, void* act, int32_t I, cudaStr
 int fcci_gemv_rowmajor(const void* W, const void* x, void* y, int32_t rows, int32_t cols, int y_fp32,
                        cudaStream_t stream);
 
+/*
+ * Fused batch-1 projection of the decode step (no reference counterpart as one call;
+ * it fuses, per layer of capture_decode_step_kernel.cu:137-274, the RMSNorm kernel
+ * :276-292, the cuBLAS GEMV of capture_decode_step.cpp:176-310, the SwiGLU kernel
+ * :294-308 and the residual add):
+ *   a    = rms_w ? fp16(x * rsqrt(mean(x^2) + eps) * rms_w) : x          (x [K])
+ *   mode 0 (store):     out[n]  = fp16(W[n] . a)                          (out [N])
+ *   mode 1 (residual):  out[n]  = fp16(out[n] + fp16(W[n] . a))
+ *   mode 2 (SwiGLU):    out[n]  = fp16(SiLU(g) * u), g = fp16(W[n] . a), u = fp16(W[N + n] . a)
+ * W row-major fp16 with leading dimension ld_w (elements); K and ld_w multiples of 8;
+ * W, x and rms_w 16-byte aligned; fp32 accumulation. In mode 1 `out` may not alias x.
+ */
+typedef struct fcci_gemv_desc {
+    const void* W;
+    int64_t ld_w;
+    int32_t N, K;
+    const void* x;
+    const void* rms_w; /* NULL: no RMSNorm prologue */
+    float eps;
+    void* out;
+    int32_t mode;
+} fcci_gemv_desc;
+
+int fcci_gemv_fused(const fcci_gemv_desc* desc, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,12 +41,13 @@ def _run(dec, prompt, steps, use_graph):
     return torch.stack(logits), toks
 
 
-def test_llama_graph_decode_matches_oracle():
+@pytest.mark.parametrize("projections", ["fused", "cublas"])
+def test_llama_graph_decode_matches_oracle(projections):
     from fully_custom_cuda_inference_lamma2_b200.llama_decode import GreedyDecoder, LlamaWeights
 
     shape = _small()
     w = LlamaWeights(shape, seed=3, std=0.05)
-    dec = GreedyDecoder(w, capacity=64, max_new_tokens=32)
+    dec = GreedyDecoder(w, capacity=64, max_new_tokens=32, projections=projections)
     g = torch.Generator().manual_seed(4)
     prompt = torch.randint(0, shape.vocab, (9,), generator=g)
     steps = 12
@@ -66,14 +67,15 @@ def test_llama_graph_decode_matches_oracle():
     assert (ref.argmax(1)[sure] == torch.tensor(toks)[sure]).all()
 
 
-def test_llama_graph_replay_equals_eager_steps():
+@pytest.mark.parametrize("projections", ["fused", "cublas"])
+def test_llama_graph_replay_equals_eager_steps(projections):
     from fully_custom_cuda_inference_lamma2_b200.llama_decode import GreedyDecoder, LlamaWeights
 
     shape = _small()
     w = LlamaWeights(shape, seed=5, std=0.05)
     prompt = torch.randint(0, shape.vocab, (7,), generator=torch.Generator().manual_seed(6)).cuda()
-    eager = GreedyDecoder(w, capacity=48, max_new_tokens=32)
-    graph = GreedyDecoder(w, capacity=48, max_new_tokens=32)
+    eager = GreedyDecoder(w, capacity=48, max_new_tokens=32, projections=projections)
+    graph = GreedyDecoder(w, capacity=48, max_new_tokens=32, projections=projections)
     le, te = _run(eager, prompt, 10, use_graph=False)
     lg, tg = _run(graph, prompt, 10, use_graph=True)
     assert te == tg
@@ -81,3 +83,54 @@ def test_llama_graph_replay_equals_eager_steps():
     # a second generation with the same graph (lengths restart on the device)
     lg2, tg2 = _run(graph, prompt, 10, use_graph=True)
     assert tg2 == tg and torch.equal(lg2, lg)
+
+
+@pytest.mark.parametrize("K", [512, 4096, 11008])
+def test_gemv_fused_modes_against_torch(K):
+    import fully_custom_cuda_inference_lamma2_b200 as pkg
+
+    cds = pkg.capture_decode_step
+    g = torch.Generator(device="cuda").manual_seed(K)
+    N = 1000
+    W = (torch.randn(2 * N, K, device="cuda", generator=g) * 0.05).half()
+    x = torch.randn(K, device="cuda", generator=g).half()
+    rw = (1 + 0.1 * torch.randn(K, device="cuda", generator=g)).half()
+    eps = 1e-5
+    # the prologue reproduces the RMSNorm kernel bit for bit
+    h = torch.empty_like(x)
+    cds.rmsnorm(x, rw, h, eps)
+    a = h.float()
+    ref = W[:N].float() @ a
+    y = torch.empty(N, dtype=torch.float16, device="cuda")
+    cds.gemv_fused(W[:N], x, y, "store", rw, eps)
+    assert torch.allclose(y.float(), ref, rtol=2e-3, atol=2e-3)
+    y0 = torch.empty(N, dtype=torch.float16, device="cuda")
+    cds.gemv_fused(W[:N], h, y0, "store")
+    assert torch.equal(y0, y), "RMSNorm prologue differs from the RMSNorm kernel"
+    # residual: out += fp16(W a)
+    base = torch.randn(N, device="cuda", generator=g).half()
+    r = base.clone()
+    cds.gemv_fused(W[:N], h, r, "residual")
+    assert torch.equal(r, (base.float() + y0.float()).half())
+    # SwiGLU over gate rows [0, N) and up rows [N, 2N), as the separate kernels on the same fp16 values
+    gu = torch.empty(2 * N, dtype=torch.float16, device="cuda")
+    cds.gemv_fused(W, h, gu, "store")
+    act_ref = torch.empty(N, dtype=torch.float16, device="cuda")
+    cds.swiglu(gu[:N], gu[N:], act_ref)
+    act = torch.empty(N, dtype=torch.float16, device="cuda")
+    cds.gemv_fused(W, x, act, "swiglu", rw, eps)
+    assert torch.equal(act, act_ref)
+    torch.cuda.synchronize()
+
+
+def test_gemv_fused_rejects_bad_shapes():
+    import fully_custom_cuda_inference_lamma2_b200 as pkg
+
+    cds = pkg.capture_decode_step
+    W = torch.zeros(8, 100, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError):
+        cds.gemv_fused(W, torch.zeros(100, dtype=torch.float16, device="cuda"),
+                       torch.zeros(8, dtype=torch.float16, device="cuda"))  # K not a multiple of 8
+    with pytest.raises(RuntimeError):
+        cds.gemv_fused(W[:, :96], torch.zeros(96, dtype=torch.float16, device="cuda"),
+                       torch.zeros(8, dtype=torch.float16, device="cuda"), "swiglu")  # needs 2N rows
