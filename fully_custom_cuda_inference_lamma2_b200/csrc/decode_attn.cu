@@ -150,6 +150,8 @@ __device__ __forceinline__ float rope_elem(float x, float partner, float2 cs, bo
 
 // Below this many tiles per CTA, uniform-length problems get pair-aligned CTA ranges.
 constexpr int kAlignBelow = 4;
+// Uniform-length pairs of at most this many tiles take one CTA each in split mode.
+constexpr int kPairTiles = 8;
 
 // Most CTAs that can hold pieces of one pair: the split grid never exceeds this.
 constexpr int kMaxPieces = 320;
@@ -221,6 +223,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
     }
+    // the next launch may start its own set-up now; everything below reads what
+    // earlier kernels wrote (lengths, queries, new rows, the arena), so wait first
+    griddep_launch_dependents();
+    griddep_wait();
 
     // ---- tile line: per-sequence tile counts and their prefix (split mode)
     bool uniform = false;
@@ -279,13 +285,19 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         // small uniform problems: use C = pairs * k CTAs with k dividing the tiles of a
         // pair, so that every range lies inside one pair (a range straddling two pairs
         // pays a second segment set-up and piece store, which dominate short ranges)
+        // and when pairs are short, or many enough to fill half the grid, one CTA per
+        // pair: no pieces and no merge, which cost more than the lost parallelism
         const long long P = (long long)B * Hkv;
-        if (uniform && N < (long long)kAlignBelow * gridDim.x && P <= (long long)gridDim.x) {
+        if (uniform && P <= (long long)gridDim.x) {
             const long long tp = N / P;
-            long long k = (long long)gridDim.x / P;
-            if (k > tp) k = tp;
-            while (k > 1 && tp % k) --k;
-            C = P * k;
+            if (tp <= kPairTiles || (2 * P >= (long long)gridDim.x && tp <= 4 * kPairTiles)) {
+                C = P;
+            } else if (N < (long long)kAlignBelow * gridDim.x) {
+                long long k = (long long)gridDim.x / P;
+                if (k > tp) k = tp;
+                while (k > 1 && tp % k) --k;
+                C = P * k;
+            }
         }
         if ((long long)blockIdx.x < C) {
             t_begin = (long long)blockIdx.x * N / C;
@@ -958,9 +970,7 @@ static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUten
         }
         if (occ >= 1 && grid > device_sm_count(dev) * occ) grid = device_sm_count(dev) * occ;
     }
-    decode_attn_kernel<D, NB><<<grid, kThreads, smem, st>>>(mk, mv, prm);
-    count_launch();
-    return set_cuda_status(cudaGetLastError());
+    return launch_pdl(decode_attn_kernel<D, NB>, dim3(grid), dim3(kThreads), smem, st, mk, mv, prm);
 }
 
 // Launch shape: persistent CTAs per SM and pipeline stages per CTA. Two CTAs

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "fcci_decode.h"
 
 namespace fcci {
@@ -33,6 +35,26 @@ int set_cuda_status(cudaError_t e);
 void count_launch();
 
 int decode_attention(const fcci_decode_desc* d, cudaStream_t stream);
+
+// Launch `kernel` with programmatic stream serialization: it may start while the
+// previous kernel of the stream finishes, and must call griddepcontrol.wait before
+// it reads that kernel's results (every kernel launched this way does).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    count_launch();
+    return set_cuda_status(e == cudaSuccess ? cudaGetLastError() : e);
+}
 int rope_append(const fcci_decode_desc* d, cudaStream_t stream);
 
 }  // namespace fcci

@@ -148,6 +148,15 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Programmatic dependent launch: let the next kernel of the stream (launched with
+// the programmatic-serialization attribute) start, and wait until every kernel this
+// one depends on has completed and its memory is visible. Without such a launch
+// both are no-ops.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Named barrier among `count` threads (count a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
