@@ -1,6 +1,6 @@
 """CPU oracle of the Llama-2-shaped greedy decode — TEST INFRASTRUCTURE ONLY.
 
-Only tests/ and bench.py's CPU-baseline leg use it, as the checker. It restates in
+Only tests/ use it, as the checker. It restates in
 torch fp32 the model the reference decodes (an HF LlamaForCausalLM: RMSNorm,
 q/k/v/o projections, rotate-half RoPE at the token's position, causal softmax
 attention, SiLU-gated MLP, tied embeddings, greedy argmax;
