@@ -297,6 +297,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 if (k > tp) k = tp;
                 while (k > 1 && tp % k) --k;
                 C = P * k;
+            } else if (20 * P * ((long long)gridDim.x / P) >= 19 * (long long)gridDim.x) {
+                // C = P * k puts CTA p*k exactly at the start of pair p (N = P * tp), so no
+                // range straddles two pairs; taken when it keeps >= 95 % of the grid busy
+                C = P * ((long long)gridDim.x / P);
             }
         }
         if ((long long)blockIdx.x < C) {
