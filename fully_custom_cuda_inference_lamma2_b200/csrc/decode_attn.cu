@@ -297,9 +297,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 if (k > tp) k = tp;
                 while (k > 1 && tp % k) --k;
                 C = P * k;
-            } else if (20 * P * ((long long)gridDim.x / P) >= 19 * (long long)gridDim.x) {
+            } else if (20 * P * ((long long)gridDim.x / P) >= 17 * (long long)gridDim.x) {
                 // C = P * k puts CTA p*k exactly at the start of pair p (N = P * tp), so no
-                // range straddles two pairs; taken when it keeps >= 95 % of the grid busy
+                // range straddles two pairs; taken when it keeps >= 85 % of the grid busy
+                // (measured faster than full-grid stream-K down to that fraction)
                 C = P * ((long long)gridDim.x / P);
             }
         }
