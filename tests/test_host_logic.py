@@ -32,6 +32,28 @@ def decompose(lens, Hkv, C):
     return pairs, t
 
 
+def effective_ctas(lens, Hkv, grid):
+    """The kernel's choice of working CTAs C in split mode (decode_attn.cu, after the
+    prologue scan): stream-K over min(grid, N), except for uniform lengths, where short
+    or numerous pairs get one CTA each, small problems pairs x k CTAs with k dividing a
+    pair's tiles, and near-full grids pairs x floor(grid / pairs) CTAs."""
+    tiles = [tiles_of(L) * Hkv for L in lens]
+    N, P = sum(tiles), len(lens) * Hkv
+    C = min(grid, N)
+    if len(set(tiles)) == 1 and P <= grid:
+        tp = N // P
+        if tp <= 8 or (2 * P >= grid and tp <= 32):
+            C = P
+        elif N < 4 * grid:
+            k = min(grid // P, tp)
+            while k > 1 and tp % k:
+                k -= 1
+            C = P * k
+        elif 20 * P * (grid // P) >= 17 * grid:
+            C = P * (grid // P)
+    return C
+
+
 @pytest.mark.parametrize("seed", range(40))
 def test_stream_k_ranges_slots_and_pieces(seed):
     rnd = random.Random(seed)
@@ -43,8 +65,11 @@ def test_stream_k_ranges_slots_and_pieces(seed):
         B = len(lens)
     else:
         lens = [rnd.choice([0, 1, 15, 64, 65, rnd.randint(1, 40000)]) for _ in range(B)]
+    if seed % 4 == 2:  # uniform lengths: the pair-aligned choices
+        lens = [rnd.choice([1, 64, 65, 300, 513, 1000, 4097, 20000])] * B
     pairs, N = decompose(lens, Hkv, grid)
-    C = min(grid, N)  # the kernel's effective grid: CTAs past N take no tiles
+    C = effective_ctas(lens, Hkv, grid)  # CTAs past C take no tiles
+    assert 1 <= C <= min(grid, N)
     owner = {}
     for c in range(C):
         lo, hi = c * N // C, (c + 1) * N // C
@@ -62,6 +87,25 @@ def test_stream_k_ranges_slots_and_pieces(seed):
             s = p + c
             assert s not in slots and s < len(pairs) + grid
             slots.add(s)
+    if len(set(lens)) == 1 and C != min(grid, N):
+        # an aligned choice: no CTA's range holds tiles of two pairs
+        pair_of = {}
+        for p, (first, n) in enumerate(pairs):
+            for t in range(first, first + n):
+                pair_of[t] = p
+        for c in range(C):
+            lo, hi = c * N // C, (c + 1) * N // C
+            assert len({pair_of[t] for t in range(lo, hi)}) <= 1
+
+
+def test_effective_ctas_on_the_measured_shapes():
+    assert effective_ctas([4096] * 32, 8, 296) == 256    # 70B shape: one CTA per (sequence, kv head)
+    assert effective_ctas([4096] * 32, 1, 296) == 288    # 8-way kv-head shard: 9 CTAs per pair
+    assert effective_ctas([513] * 1, 32, 296) == 288     # 1 x 32 heads x 513 keys: 9 tiles per pair, k = 9
+    assert effective_ctas([300] * 1, 32, 296) == 32      # short pairs (5 tiles): one CTA each
+    assert effective_ctas([1001] * 1, 32, 296) == 256    # 16 tiles per pair, fewer than 4 per CTA: k = 8
+    assert effective_ctas([100, 200], 32, 296) == 192    # mixed lengths: stream-K over all 192 tiles
+    assert effective_ctas([4096] * 64, 32, 296) == 296   # more pairs than CTAs: stream-K
 
 
 def test_partition_sequences_balances_bytes():
