@@ -9,6 +9,7 @@
 
 #include "fcci_decode.h"
 #include "fcci_internal.h"
+#include "ptx.cuh"
 
 namespace fcci {
 
@@ -161,3 +162,42 @@ void capture_decode_host(const int64_t* ctrl_input, void* arena_k, void* arena_v
 }
 
 }  // extern "C"
+
+// Self-test of the bounded wait every pipeline wait of the kernels goes through:
+// one CTA waits on an mbarrier that nothing arrives on. The wait must give up after
+// the limit and report it, the kernel must return, and the context stays usable.
+namespace fcci {
+__global__ void bounded_wait_probe_kernel(uint64_t limit_ns, uint32_t* out) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const uint64_t t0 = global_timer_ns();
+    const bool ok = mbar_wait_bounded(&bar, 0, &abort_flag, limit_ns);  // no arrival ever comes
+    const uint64_t t1 = global_timer_ns();
+    if (threadIdx.x == 0) {
+        out[0] = ok ? 0u : FCCI_DEV_ERR_TIMEOUT;
+        out[1] = (uint32_t)((t1 - t0) / 1000000ull);  // milliseconds waited
+    }
+}
+}  // namespace fcci
+
+extern "C" int fcci_selftest_bounded_wait(uint64_t limit_ns, uint32_t* result, cudaStream_t stream) {
+    if (!result) return fcci::set_status(FCCI_EINVAL, "fcci_selftest_bounded_wait: result is NULL");
+    if (limit_ns == 0 || limit_ns > 1000000000ull)
+        return fcci::set_status(FCCI_EINVAL, "fcci_selftest_bounded_wait: limit must be in (0, 1 s]");
+    uint32_t* d = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d), 2 * sizeof(uint32_t), stream);
+    if (e != cudaSuccess) return fcci::set_cuda_status(e);
+    fcci::bounded_wait_probe_kernel<<<1, 32, 0, stream>>>(limit_ns, d);
+    fcci::count_launch();
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(result, d, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    cudaFreeAsync(d, stream);
+    return fcci::set_cuda_status(e);
+}

@@ -176,6 +176,13 @@ const char* fcci_last_error_string(void);
 /* Number of kernel launches this library has issued (process-wide counter). */
 uint64_t fcci_launch_count(void);
 
+/* Self-test of failure detection (no reference counterpart): one CTA runs the bounded
+ * mbarrier wait that every pipeline wait of these kernels uses, on a barrier nothing
+ * arrives on, with limit_ns in (0, 1 s]. result[0] receives FCCI_DEV_ERR_TIMEOUT when
+ * the wait gave up (the expected outcome), result[1] the milliseconds it waited.
+ * Synchronises `stream`. Nothing faults or hangs: the kernel returns after the limit. */
+int fcci_selftest_bounded_wait(uint64_t limit_ns, uint32_t* result, cudaStream_t stream);
+
 /*
  * Reference symbol (custom_kernels/attn_varlen_kernel.cu:88-99).
  * q [H,D], k/v [H,T,D] contiguous, ctx_out [H,D]; attention of each head over
