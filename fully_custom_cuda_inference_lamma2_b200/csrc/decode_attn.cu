@@ -178,6 +178,8 @@ struct Layout {
 template <int D, int NB>
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                const __grid_constant__ CUtensorMap tmV,
+                                                               const __grid_constant__ CUtensorMap tmK64,
+                                                               const __grid_constant__ CUtensorMap tmV64,
                                                                const Params p) {
     using LY = Layout<D, NB>;
     constexpr int G8 = LY::G8;
@@ -222,6 +224,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     if (tid == kConsumerThreads) {
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
+        prefetch_tmap(&tmK64);
+        prefetch_tmap(&tmV64);
     }
     // the next launch may start its own set-up now; everything below reads what
     // earlier kernels wrote (lengths, queries, new rows, the arena), so wait first
@@ -353,13 +357,24 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 uint8_t* vdst = kdst + KT;
                 const int row0 = si.tok_base + kTileKeys * j;
                 const int c3 = p.cu_seqlens ? 0 : b;
-                for (int g = 0; g < ngr; ++g) {
+                if (nv == kTileKeys) {
+                    // a full tile: one 64-row box per 64-column half (the same swizzled
+                    // layout as four 16-row boxes, in a quarter of the TMA instructions)
 #pragma unroll
                     for (int hf = 0; hf < HALVES; ++hf) {
-                        tma_load_4d(kdst + hf * kHalfTileBytes + g * kBoxBytes, &tmK, hf * 64, row0 + kGroupKeys * g, h,
-                                    c3, &full[s], pol);
-                        tma_load_4d(vdst + hf * kHalfTileBytes + g * kBoxBytes, &tmV, hf * 64, row0 + kGroupKeys * g, h,
-                                    c3, &full[s], pol);
+                        tma_load_4d(kdst + hf * kHalfTileBytes, &tmK64, hf * 64, row0, h, c3, &full[s], pol);
+                        tma_load_4d(vdst + hf * kHalfTileBytes, &tmV64, hf * 64, row0, h, c3, &full[s], pol);
+                    }
+                } else {
+                    // the last tile of a pair: only the 16-row boxes holding valid keys
+                    for (int g = 0; g < ngr; ++g) {
+#pragma unroll
+                        for (int hf = 0; hf < HALVES; ++hf) {
+                            tma_load_4d(kdst + hf * kHalfTileBytes + g * kBoxBytes, &tmK, hf * 64,
+                                        row0 + kGroupKeys * g, h, c3, &full[s], pol);
+                            tma_load_4d(vdst + hf * kHalfTileBytes + g * kBoxBytes, &tmV, hf * 64,
+                                        row0 + kGroupKeys * g, h, c3, &full[s], pol);
+                        }
                     }
                 }
                 ++issued;
@@ -910,13 +925,13 @@ int encode_f16_sw128(CUtensorMap* map, const void* base, int rank, const uint64_
     return r == CUDA_SUCCESS ? FCCI_OK : FCCI_ETMAP;
 }
 
-// 4-D map (head_dim, token, kv head, sequence) over an fp16 arena; 64 x 16 boxes.
-// Strides in elements.
+// 4-D map (head_dim, token, kv head, sequence) over an fp16 arena; 64-column boxes of
+// box_rows keys. Strides in elements.
 static int encode_kv_map(CUtensorMap* map, const void* base, int D, int64_t tokens, int Hkv, int Bdim, int64_t st,
-                         int64_t sh, int64_t sb) {
+                         int64_t sh, int64_t sb, int box_rows = kGroupKeys) {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)tokens, (uint64_t)Hkv, (uint64_t)Bdim};
     const int64_t sbytes[3] = {st * 2, sh * 2, sb * 2};
-    const uint32_t box[4] = {64, (uint32_t)kGroupKeys, 1, 1};
+    const uint32_t box[4] = {64, (uint32_t)box_rows, 1, 1};
     return encode_f16_sw128(map, base, 4, dims, sbytes, box);
 }
 
@@ -939,7 +954,8 @@ WorkspaceLayout workspace_layout(int B, int Hq, int Hkv, int D, int grid) {
 int max_grid(int dev) { return device_sm_count(dev) * kMaxCtasPerSm; }
 
 template <int D, int NB>
-static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUtensorMap& mv, int grid, cudaStream_t st,
+static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mk64,
+                           const CUtensorMap& mv64, int grid, cudaStream_t st,
                            int dev) {
     using LY = Layout<D, NB>;
     static std::once_flag flags[128];
@@ -975,7 +991,7 @@ static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUten
         }
         if (occ >= 1 && grid > device_sm_count(dev) * occ) grid = device_sm_count(dev) * occ;
     }
-    return launch_pdl(decode_attn_kernel<D, NB>, dim3(grid), dim3(kThreads), smem, st, mk, mv, prm);
+    return launch_pdl(decode_attn_kernel<D, NB>, dim3(grid), dim3(kThreads), smem, st, mk, mv, mk64, mv64, prm);
 }
 
 // Launch shape: persistent CTAs per SM and pipeline stages per CTA. Two CTAs
@@ -1133,16 +1149,19 @@ int decode_attention(const fcci_decode_desc* d, cudaStream_t stream) {
 
     CUtensorMap mk, mv;
     const int Bdim = p.cu_seqlens ? 1 : p.B;
+    CUtensorMap mk64, mv64;
     rc = encode_kv_map(&mk, p.k_cache, d->D, p.capacity, p.Hkv, Bdim, p.k_st, p.k_sh, p.k_sb);
     if (!rc) rc = encode_kv_map(&mv, p.v_cache, d->D, p.capacity, p.Hkv, Bdim, p.v_st, p.v_sh, p.v_sb);
+    if (!rc) rc = encode_kv_map(&mk64, p.k_cache, d->D, p.capacity, p.Hkv, Bdim, p.k_st, p.k_sh, p.k_sb, kTileKeys);
+    if (!rc) rc = encode_kv_map(&mv64, p.v_cache, d->D, p.capacity, p.Hkv, Bdim, p.v_st, p.v_sh, p.v_sb, kTileKeys);
     if (rc) return set_status(rc, "fcci_decode_attention: cuTensorMapEncodeTiled rejected the arena layout");
 
     switch (d->D * 10 + NB) {
-        case 641: return launch_decode_t<64, 1>(p, mk, mv, grid, stream, dev);
-        case 642: return launch_decode_t<64, 2>(p, mk, mv, grid, stream, dev);
-        case 1281: return launch_decode_t<128, 1>(p, mk, mv, grid, stream, dev);
-        case 1282: return launch_decode_t<128, 2>(p, mk, mv, grid, stream, dev);
-        case 2561: return launch_decode_t<256, 1>(p, mk, mv, grid, stream, dev);
+        case 641: return launch_decode_t<64, 1>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 642: return launch_decode_t<64, 2>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 1281: return launch_decode_t<128, 1>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 1282: return launch_decode_t<128, 2>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 2561: return launch_decode_t<256, 1>(p, mk, mv, mk64, mv64, grid, stream, dev);
         default: return set_status(FCCI_EUNSUPPORTED, "fcci_decode_attention: unsupported head_dim");
     }
 }
