@@ -54,6 +54,7 @@ constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kBoxBytes = kGroupKeys * 128;  // 16 rows x 64 fp16
 constexpr int kHalfTileBytes = kTileKeys * 128;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any healthy wait
+constexpr int kCoopPieces = 6;  // pieces per pair from which the piece CTAs merge a slice each
 constexpr uint64_t kDrainLimitNs = 500000000ull;
 constexpr int kConsumerBar = 1;
 
@@ -657,13 +658,18 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 named_bar_sync(kConsumerBar, kConsumerThreads);
 
                 const int pidx = b * Hkv + h;
-                bool whole = true;
+                bool whole = true, coop = false;
                 int c0 = 0, c1 = 0;
                 if (p.split) {
                     const long long pfirst = tile_base[b] + (long long)h * tiles;
                     c0 = cta_of_tile(pfirst, N, C);
                     c1 = cta_of_tile(pfirst + tiles - 1, N, C);
                     whole = (c0 == c1);
+                    // every piece of the pair ends its CTA's range (pair-aligned ranges): the
+                    // pieces' CTAs can wait for one another and merge a slice each, as no CTA
+                    // has a later segment that the wait would hold up. Taken from kCoopPieces
+                    // pieces up (measured: 9 pieces -9 % per launch, 4 even, 2 +5 %)
+                    coop = !whole && c1 - c0 + 1 >= kCoopPieces && (pfirst + tiles == ((long long)c1 + 1) * N / C);
                 }
                 const int slot = pidx + blockIdx.x;
                 __half* ob = p.out + (int64_t)b * p.o_sb;
@@ -694,7 +700,60 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     }
                 }
                 named_bar_sync(kConsumerBar, kConsumerThreads);
-                if (!whole) {
+                if (coop) {
+                    // ---- all pieces of the pair arrive (counter to nparts), then each CTA
+                    //      merges its slice of the G x D outputs over every piece, in piece
+                    //      order with the running log-sum-exp of the single-merger path below
+                    //      (same arithmetic per element); the second round of increments
+                    //      (to 2 nparts) tells the last CTA to reset the counter
+                    const int nparts = c1 - c0 + 1;
+                    if (ctid == 0) {
+                        __threadfence();
+                        atomicAdd(&p.pair_cnt[pidx], 1u);
+                        volatile unsigned* cnt = &p.pair_cnt[pidx];
+                        int ok = 1;
+                        if (*cnt < (unsigned)nparts) {
+                            const uint64_t t0 = global_timer_ns();
+                            while (*cnt < (unsigned)nparts) {
+                                if (global_timer_ns() - t0 > kWaitLimitNs) {
+                                    ok = 0;
+                                    set_error(p, FCCI_DEV_ERR_TIMEOUT);
+                                    break;
+                                }
+                            }
+                        }
+                        __threadfence();
+                        misc[1] = ok;
+                    }
+                    named_bar_sync(kConsumerBar, kConsumerThreads);
+                    if (misc[1]) {
+                        const float* pl = p.part_lse + (size_t)(pidx + c0) * G;
+                        const float* po = p.part_o + (size_t)(pidx + c0) * G * D;
+                        const int E = G * D, r = (int)blockIdx.x - c0;
+                        const int lo = (int)((long long)r * E / nparts), hi = (int)((long long)(r + 1) * E / nparts);
+                        for (int e = lo + ctid; e < hi; e += kConsumerThreads) {
+                            const int hh = e / D;
+                            const int d = e - hh * D;
+                            float Mx = -INFINITY, Wt = 0.f, Ov = 0.f;
+                            for (int c = 0; c < nparts; ++c) {
+                                const float lse = __ldcg(pl + (size_t)c * G + hh);
+                                const float ov = __ldcg(po + (size_t)c * G * D + e);
+                                if (lse != -INFINITY) {
+                                    const float mn = fmaxf(Mx, lse);
+                                    const float a = ex2(Mx - mn), wgt = ex2(lse - mn);
+                                    Wt = Wt * a + wgt;
+                                    Ov = Ov * a + wgt * ov;
+                                    Mx = mn;
+                                }
+                            }
+                            const float inv = Wt > 0.f ? 1.f / Wt : 0.f;
+                            ob[(int64_t)(h * G + hh) * p.o_sh + d] = __float2half_rn(Ov * inv);
+                        }
+                    }
+                    named_bar_sync(kConsumerBar, kConsumerThreads);
+                    if (ctid == 0 && atomicAdd(&p.pair_cnt[pidx], 1u) == 2u * (unsigned)nparts - 1u)
+                        atomicExch(&p.pair_cnt[pidx], 0u);
+                } else if (!whole) {
                     // ---- the last piece of a cut pair merges every piece's (o, lse).
                     //      The barrier above orders this CTA's piece stores before thread
                     //      0's fence and counter increment (release); the last arriver

@@ -216,6 +216,27 @@ def test_decode_long_split_kv(av):
     assert_close(got["out"], want["ctx"], "split-kv 32k")
 
 
+@pytest.mark.parametrize("B,Hkv,G,T", [(32, 1, 8, 4095), (32, 2, 8, 4095), (1, 32, 1, 1000), (4, 8, 8, 4095)])
+def test_decode_pair_aligned_pieces(av, B, Hkv, G, T):
+    """Uniform lengths whose pairs the kernel cuts into pair-aligned pieces (the kv-head
+    shards of the 70B shape, and pairs x k CTAs with k dividing a pair's tiles): the piece
+    CTAs merge a slice each. Calls alternate with ragged lengths (stream-K pieces and the
+    single-merger path) on one workspace, so the pair counters must come back to zero."""
+    D, cap = 128, T + 8
+    ws = av.make_workspace(B, Hkv * G, Hkv, D)
+    for i, lens in enumerate([[T] * B, [max(1, T - 977 * b % T) for b in range(B)], [T] * B]):
+        q, kn, vn, kc, vc, lt, _ = make_case(B, Hkv, G, D, lens, cap, seed=700 + i)
+        dk, dv, dl = kc.to(DEV), vc.to(DEV), lt.to(DEV)
+        out = torch.full((B, Hkv * G, D), float("nan"), dtype=torch.float16, device=DEV)
+        av.decode(q.to(DEV), dk, dv, out, k_new=kn.to(DEV), v_new=vn.to(DEV), seq_lens=dl, advance=True,
+                  workspace=ws, split=True)
+        torch.cuda.synchronize()
+        assert av.read_error(ws) == 0
+        want = O.decode_step(q, kc, vc, lt, k_new=kn, v_new=vn)
+        assert_close(out.cpu(), want["ctx"], f"B={B} Hkv={Hkv} G={G} call {i}")
+        assert dl.cpu().tolist() == [t + 1 for t in lens]
+
+
 def test_decode_capacity_overflow_sets_error(av):
     lens = [10, 400, 20]  # 400 + 1 > cap 400
     B, Hkv, G, D, cap = 3, 2, 4, 128, 400

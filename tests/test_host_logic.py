@@ -108,6 +108,54 @@ def test_effective_ctas_on_the_measured_shapes():
     assert effective_ctas([4096] * 64, 32, 296) == 296   # more pairs than CTAs: stream-K
 
 
+COOP_PIECES = 6  # decode_attn.cu kCoopPieces
+
+
+def merge_mode(pairs, N, C, p):
+    """How pair p's pieces are merged (decode_attn.cu, segment end): 'whole' (one CTA),
+    'slices' (every piece ends its CTA's range and there are at least COOP_PIECES pieces:
+    the piece CTAs wait for one another and merge a slice each) or 'single' (the last
+    arriving piece merges all)."""
+    first, n = pairs[p]
+    c0, c1 = cta_of_tile(first, N, C), cta_of_tile(first + n - 1, N, C)
+    if c0 == c1:
+        return "whole"
+    if c1 - c0 + 1 >= COOP_PIECES and first + n == (c1 + 1) * N // C:
+        return "slices"
+    return "single"
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_slice_merge_never_holds_up_a_later_segment(seed):
+    rnd = random.Random(1000 + seed)
+    Hkv = rnd.choice([1, 2, 8, 32])
+    grid = rnd.choice([148, 296])
+    B = rnd.randint(1, 40)
+    lens = [rnd.choice([4096, 1000, 513, rnd.randint(1, 40000)])] * B if seed % 2 else \
+        [rnd.randint(1, 40000) for _ in range(B)]
+    pairs, N = decompose(lens, Hkv, grid)
+    C = effective_ctas(lens, Hkv, grid)
+    for p, (first, n) in enumerate(pairs):
+        if merge_mode(pairs, N, C, p) != "slices":
+            continue
+        # every piece CTA's range ends inside this pair: waiting there delays nothing else
+        for c in range(cta_of_tile(first, N, C), cta_of_tile(first + n - 1, N, C) + 1):
+            assert first < (c + 1) * N // C <= first + n
+
+
+def test_merge_modes_on_the_measured_shapes():
+    def modes(lens, Hkv, grid=296):
+        pairs, N = decompose(lens, Hkv, grid)
+        C = effective_ctas(lens, Hkv, grid)
+        return {merge_mode(pairs, N, C, p) for p in range(len(pairs))}
+    assert modes([4096] * 32, 8) == {"whole"}     # 70B shape on one GPU: one CTA per pair
+    assert modes([4096] * 32, 1) == {"slices"}    # 8-way kv-head shard: 9 pieces per pair
+    assert modes([4096] * 32, 2) == {"single"}    # 4-way shard: 4 pieces per pair
+    assert modes([4096] * 32, 4) == {"single"}    # 2-way shard: 2 pieces per pair
+    assert modes([32768] * 4, 8) == {"slices"}    # 4 x 32k keys
+    assert modes([1001], 32) == {"slices"}        # 1 x 32 heads x 1001 keys: 8 pieces per pair
+
+
 def test_partition_sequences_balances_bytes():
     rnd = random.Random(3)
     lens = [rnd.randint(128, 8192) for _ in range(64)]
