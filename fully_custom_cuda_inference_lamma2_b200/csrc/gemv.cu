@@ -20,6 +20,7 @@
 #include "fcci_compat.h"
 #include "fcci_decode.h"
 #include "fcci_internal.h"
+#include "ptx.cuh"
 
 namespace fcci {
 namespace gv {
@@ -60,6 +61,9 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __half* __restrict
     __shared__ float red[kWarps];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nchunk = K >> 3;
+    // a programmatic dependent of this launch (the decode-attention kernel) may start its
+    // set-up now; it waits for this grid's completion before reading anything
+    griddep_launch_dependents();
 
     // ---- prologue: the input vector (normalised when asked) into shared memory
     if (NORM) {
