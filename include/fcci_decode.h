@@ -162,7 +162,9 @@ int fcci_rope_append(const fcci_decode_desc* desc, cudaStream_t stream);
 size_t fcci_decode_workspace_bytes(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int device);
 /* Zero the counters and error word of a fresh workspace (stream-ordered). */
 int fcci_decode_workspace_init(void* workspace, size_t bytes, cudaStream_t stream);
-/* Copy the device error word to *flags (synchronises `stream`); clear it when clear != 0. */
+/* Copy the device error word to *flags (synchronises `stream`); clear it when clear != 0.
+ * After FCCI_DEV_ERR_TIMEOUT the workspace's merge counters may be left mid-count:
+ * run fcci_decode_workspace_init on it before its next use. */
 int fcci_decode_read_error(void* workspace, uint32_t* flags, int clear, cudaStream_t stream);
 
 /* Tuning hook for measurements: pipeline stages per CTA (2..8) and persistent
