@@ -248,7 +248,7 @@ def run_step(st, gather=None):
     L = arena.layers
     for l in range(L):
         st["fcci"].decode_attention(arena, l, st["q"][l], st["out"][l], k_new=st["kn"][l], v_new=st["vn"][l],
-                                    advance=(l == L - 1))
+                                    advance=(l == L - 1), prefetch_kv=st["prefetch_kv"])
         if gather is not None:
             gather(l)
 
@@ -257,6 +257,10 @@ def ours(args):
     world, rank, local = dist_setup(args.gpus)
     w = workload(args.workload, args.layers)
     st = build_state(w, world, rank)
+    # each layer's launch may read its lengths and first K/V tiles while the previous
+    # layer's launch drains: that launch writes only its own arena, ctx and workspace,
+    # and only the last layer advances seq_lens (each step starts with a copy)
+    st["prefetch_kv"] = not args.no_prefetch_kv
     L, D = w["layers"], w["D"]
     gather = None
     if args.gather_ctx and world > 1:
@@ -357,6 +361,7 @@ def ours(args):
             "kv_len": (w["lens"][0] if len(set(w["lens"])) == 1 else "seeded U[128,8192]"), "layers": L,
             "parallelism": ("kv-head shards x%d" % world) if not w["packed"] else ("sequence shards x%d" % world),
             "gather_ctx": bool(args.gather_ctx and world > 1),
+            "prefetch_kv": st["prefetch_kv"],
             "l2": "no flush: arena %.1f GB per GPU > 126 MB L2" % (st["arena"].k.numel() * 4 / 1e9),
         },
         "tokens_per_s": round(tokens_per_s, 1),
@@ -409,7 +414,8 @@ def e2e_run(st, args, L):
                 ready[l].record(copy_in)
         for l in range(L):
             comp.wait_event(ready[l])
-            st["fcci"].decode_attention(arena, l, dq[l], dout[l], k_new=dkn[l], v_new=dvn[l], advance=(l == L - 1))
+            st["fcci"].decode_attention(arena, l, dq[l], dout[l], k_new=dkn[l], v_new=dvn[l], advance=(l == L - 1),
+                                        prefetch_kv=st["prefetch_kv"])
             done[l].record(comp)
             with torch.cuda.stream(copy_out):
                 copy_out.wait_event(done[l])
@@ -1044,6 +1050,8 @@ def main():
                     choices=["gqa70b", "gqa70b_32k", "varlen7b", "mha7b", "prefill16", "llama7b"])
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--gather-ctx", action="store_true")
+    ap.add_argument("--no-prefetch-kv", action="store_true",
+                    help="decode launches read nothing before the previous launch finishes")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -71,14 +71,21 @@ class KVArena:
 def decode_attention(arena: KVArena, layer: int, q: torch.Tensor, out: torch.Tensor, *,
                      k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None,
                      advance: bool = False, scale: Optional[float] = None, rope_theta: float = 10000.0,
-                     rotary_dim: int = -1, q_rot_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     rotary_dim: int = -1, q_rot_out: Optional[torch.Tensor] = None,
+                     prefetch_kv: bool = False) -> torch.Tensor:
     """One decode-attention step of `layer`: RoPE + append at T_b (when k_new is given) and
-    split-KV attention, on the current stream, without allocation or host sync."""
+    split-KV attention, on the current stream, without allocation or host sync.
+
+    prefetch_kv: read the lengths and the first cached K/V tiles before waiting for the
+    previous kernel on the stream (FCCI_DECODE_PREFETCH_KV). Only when no kernel that may
+    still be running writes seq_lens or this layer's cached rows, e.g. right after the
+    projection that produced q/k_new/v_new, or after another layer's decode step that
+    does not advance."""
     k, v = arena.layer(layer)
     attn_varlen.decode(q, k, v, out, k_new=k_new, v_new=v_new, seq_lens=arena.seq_lens,
                        cu_seqlens=arena.cu_seqlens, scale=-1.0 if scale is None else float(scale),
                        rope_theta=rope_theta, rotary_dim=rotary_dim, advance=advance,
-                       workspace=arena.workspace, q_rot_out=q_rot_out, split=True)
+                       workspace=arena.workspace, q_rot_out=q_rot_out, split=True, prefetch_kv=prefetch_kv)
     return out
 
 

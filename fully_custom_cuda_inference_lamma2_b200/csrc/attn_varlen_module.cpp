@@ -88,7 +88,7 @@ void forward_out(at::Tensor q, at::Tensor k, at::Tensor v, int64_t seq_len, doub
 void decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor out, c10::optional<at::Tensor> k_new,
             c10::optional<at::Tensor> v_new, c10::optional<at::Tensor> seq_lens, c10::optional<at::Tensor> cu_seqlens,
             int64_t fixed_len, double scale, double rope_theta, int64_t rotary_dim, bool advance,
-            c10::optional<at::Tensor> workspace, c10::optional<at::Tensor> q_rot_out, bool split) {
+            c10::optional<at::Tensor> workspace, c10::optional<at::Tensor> q_rot_out, bool split, bool prefetch_kv) {
     check_half_cuda(q, "q");
     check_half_cuda(k_cache, "k_cache");
     check_half_cuda(v_cache, "v_cache");
@@ -187,6 +187,7 @@ void decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor out
     else if (split || advance) ws = make_workspace(B, Hq, Hkv, D, q.device());
     if (ws.defined()) bind_workspace(d, ws);
     d.split = split ? 1 : 0;
+    d.flags = prefetch_kv ? FCCI_DECODE_PREFETCH_KV : 0u;
     check_rc(fcci_decode_attention(&d, current_stream()), "attn_varlen.decode");
 }
 
@@ -389,7 +390,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("v_new") = py::none(), py::arg("seq_lens") = py::none(), py::arg("cu_seqlens") = py::none(),
           py::arg("fixed_len") = -1, py::arg("scale") = -1.0, py::arg("rope_theta") = 10000.0,
           py::arg("rotary_dim") = -1, py::arg("advance") = false, py::arg("workspace") = py::none(),
-          py::arg("q_rot_out") = py::none(), py::arg("split") = true);
+          py::arg("q_rot_out") = py::none(), py::arg("split") = true, py::arg("prefetch_kv") = false);
     m.def("rope_append", &rope_append, "RoPE(q,k_new) at T and append of k/v at T (no attention)", py::arg("q"),
           py::arg("k_new"), py::arg("v_new"), py::arg("k_cache"), py::arg("v_cache"), py::arg("seq_lens"),
           py::arg("cu_seqlens") = py::none(), py::arg("rope_theta") = 10000.0, py::arg("rotary_dim") = -1,

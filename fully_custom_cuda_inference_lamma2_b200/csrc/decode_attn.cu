@@ -82,6 +82,7 @@ struct Params {
     int32_t advance;
     int32_t append;
     int32_t split;
+    int32_t prefetch_kv;  // FCCI_DECODE_PREFETCH_KV: lengths and the first stages before griddepcontrol.wait
     int32_t B, Hq, Hkv, G;
     int32_t stages;
     uint32_t* err;
@@ -228,10 +229,13 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         prefetch_tmap(&tmK64);
         prefetch_tmap(&tmV64);
     }
-    // the next launch may start its own set-up now; everything below reads what
-    // earlier kernels wrote (lengths, queries, new rows, the arena), so wait first
+    // the next launch may start its own set-up now. Everything below reads what
+    // earlier kernels wrote (lengths, queries, new rows, the arena), so wait first;
+    // with prefetch_kv the caller guarantees that no kernel still running writes the
+    // lengths or the cached rows, and only the reads of q / k_new / v_new (consumers)
+    // and the producer's loads after its first S stages wait
     griddep_launch_dependents();
-    griddep_wait();
+    if (!p.prefetch_kv) griddep_wait();
 
     // ---- tile line: per-sequence tile counts and their prefix (split mode)
     bool uniform = false;
@@ -346,6 +350,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
             for (int it = 0; it < ntiles; ++it) {
                 const int s = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
+                if (it == S && p.prefetch_kv) griddep_wait();
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag, kWaitLimitNs)) {
                     *abort_flag = 1;
                     set_error(p, FCCI_DEV_ERR_TIMEOUT);
@@ -400,6 +405,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         }
     } else {
         // ============================================================ consumers
+        if (p.prefetch_kv) griddep_wait();
         const int w = warp;
         const int ctid = tid;  // 0..127
         const int g = lane >> 2, t4 = lane & 3;
@@ -1091,7 +1097,10 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 static int fill_params(const fcci_decode_desc* d, Params& p, bool attention) {
     auto bad = [](int code, const char* why) { return set_status(code, why); };
     if (!d) return bad(FCCI_EINVAL, "descriptor is NULL");
-    if (d->abi_version != FCCI_DECODE_ABI_VERSION) return bad(FCCI_EINVAL, "abi_version mismatch");
+    if (d->abi_version != 1 && d->abi_version != FCCI_DECODE_ABI_VERSION)
+        return bad(FCCI_EINVAL, "abi_version mismatch");
+    const uint32_t flags = d->abi_version >= 2 ? d->flags : 0u;
+    if (flags & ~FCCI_DECODE_PREFETCH_KV) return bad(FCCI_EINVAL, "unknown bits in flags");
     if (d->B <= 0 || d->Hq <= 0 || d->Hkv <= 0 || d->Hq % d->Hkv != 0)
         return bad(FCCI_EINVAL, "B, Hq, Hkv must be positive and Hq a multiple of Hkv");
     if (d->D != 64 && d->D != 128 && d->D != 256) return bad(FCCI_EUNSUPPORTED, "unsupported head_dim (64, 128 or 256)");
@@ -1154,6 +1163,7 @@ static int fill_params(const fcci_decode_desc* d, Params& p, bool attention) {
     p.advance = d->advance;
     p.append = d->k_new ? 1 : 0;
     p.split = d->split ? 1 : 0;
+    p.prefetch_kv = (flags & FCCI_DECODE_PREFETCH_KV) ? 1 : 0;
     p.B = d->B;
     p.Hq = d->Hq;
     p.Hkv = d->Hkv;

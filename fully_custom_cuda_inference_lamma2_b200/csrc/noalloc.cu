@@ -11,6 +11,7 @@
 // results, merge counters, error word) comes from here.
 #include <cuda_runtime.h>
 #include <stdio.h>
+#include <string.h>
 
 #include <mutex>
 
@@ -68,7 +69,10 @@ extern "C" int fcci_decode_attention_noalloc(const fcci_decode_desc* desc, cudaS
         fcci::workspace_layout(desc->B, desc->Hq, desc->Hkv, desc->D, fcci::max_grid(dev));
     e = cudaMemsetAsync(scratch, 0, L.zero_bytes, stream);
     if (e != cudaSuccess) return fcci::set_cuda_status(e);
-    fcci_decode_desc d = *desc;
+    // a version-1 descriptor ends before `flags`: copy only what the caller has
+    fcci_decode_desc d;
+    memset(&d, 0, sizeof(d));
+    memcpy(&d, desc, desc->abi_version >= 2 ? sizeof(d) : offsetof(fcci_decode_desc, flags));
     d.workspace = scratch;
     d.workspace_bytes = FCCI_NOALLOC_SCRATCH_BYTES;
     return fcci_decode_attention(&d, stream);

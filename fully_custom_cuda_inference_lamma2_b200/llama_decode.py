@@ -139,7 +139,7 @@ class GreedyDecoder:
         k = self.qkv[Hq * D: (Hq + Hkv) * D].view(1, Hkv, D)
         v = self.qkv[(Hq + Hkv) * D:].view(1, Hkv, D)
         decode_attention(self.arena, l, q, self.ctx.view(1, Hq, D), k_new=k, v_new=v,
-                         advance=(l == s.layers - 1), rope_theta=s.rope_theta)
+                         advance=(l == s.layers - 1), rope_theta=s.rope_theta, prefetch_kv=True)
         torch.mv(w.w_o[l], self.ctx, out=self.tmp)
         self.x.add_(self.tmp)
         capture_decode_step.rmsnorm(self.x, w.rms_post[l], self.h, s.eps)
@@ -160,7 +160,7 @@ class GreedyDecoder:
         k = self.qkv[Hq * D: (Hq + Hkv) * D].view(1, Hkv, D)
         v = self.qkv[(Hq + Hkv) * D:].view(1, Hkv, D)
         decode_attention(self.arena, l, q, self.ctx.view(1, Hq, D), k_new=k, v_new=v,
-                         advance=(l == s.layers - 1), rope_theta=s.rope_theta)
+                         advance=(l == s.layers - 1), rope_theta=s.rope_theta, prefetch_kv=True)
         gemv(w.w_o[l], self.ctx, self.x, "residual")
         gemv(w.w_gu[l], self.x, self.act, "swiglu", w.rms_post[l], s.eps)
         gemv(w.w_down[l], self.act, self.x, "residual")

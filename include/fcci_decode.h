@@ -57,7 +57,8 @@
 extern "C" {
 #endif
 
-#define FCCI_DECODE_ABI_VERSION 1
+/* 2 adds the trailing `flags` field; descriptors of version 1 (no flags) are still accepted */
+#define FCCI_DECODE_ABI_VERSION 2
 
 /* status codes */
 #define FCCI_OK 0
@@ -98,9 +99,22 @@ extern "C" {
  *                      (sequence, kv head) pair, no partials).
  *   split              0: one CTA per (sequence, kv-head) pair; 1: persistent
  *                      stream-K split over all SMs with last-arriver combine.
+ *   flags              (abi_version >= 2) bit set of FCCI_DECODE_* below.
  *
  * Calls that share a workspace must not overlap on the GPU.
+ *
+ * FCCI_DECODE_PREFETCH_KV: the kernel is launched as a programmatic dependent of
+ * the kernel before it on the stream, and by default reads nothing until that
+ * kernel has finished. With this flag it reads seq_lens, cu_seqlens and its first
+ * pipeline stages of cached keys and values (rows below T_b) before that wait, so
+ * those loads overlap the previous kernel's last CTAs; q, k_new and v_new are
+ * still read after it. Set it only when no kernel that can still be running when
+ * this one starts writes seq_lens, cu_seqlens or those arena rows: for example a
+ * chain of decode steps over different layers' arenas where only the last one
+ * advances seq_lens (and the next step starts with a copy or a non-dependent
+ * launch), or a decode step right after the projection that produced q/k/v.
  */
+#define FCCI_DECODE_PREFETCH_KV 1u
 typedef struct fcci_decode_desc {
     int32_t abi_version; /* FCCI_DECODE_ABI_VERSION */
     int32_t B, Hq, Hkv, D;
@@ -128,6 +142,7 @@ typedef struct fcci_decode_desc {
     int32_t split;
     void* workspace;
     size_t workspace_bytes;
+    uint32_t flags; /* abi_version >= 2 */
 } fcci_decode_desc;
 
 int fcci_decode_attention(const fcci_decode_desc* desc, cudaStream_t stream);

@@ -7,24 +7,33 @@ import os
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(ROOT, "fully_custom_cuda_inference_lamma2_b200", "libfcci_decode.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
+PREFETCH_KV = 1
 
 c_i32, c_i64, c_vp, c_f32, c_sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t
 
 
+_DESC_V1_FIELDS = [
+    ("abi_version", c_i32), ("B", c_i32), ("Hq", c_i32), ("Hkv", c_i32), ("D", c_i32),
+    ("q", c_vp), ("q_stride_b", c_i64), ("q_stride_h", c_i64),
+    ("k_new", c_vp), ("k_new_stride_b", c_i64), ("k_new_stride_h", c_i64),
+    ("v_new", c_vp), ("v_new_stride_b", c_i64), ("v_new_stride_h", c_i64),
+    ("k_cache", c_vp), ("k_stride_b", c_i64), ("k_stride_h", c_i64), ("k_stride_t", c_i64),
+    ("v_cache", c_vp), ("v_stride_b", c_i64), ("v_stride_h", c_i64), ("v_stride_t", c_i64),
+    ("capacity", c_i32), ("cu_seqlens", c_vp), ("seq_lens", c_vp), ("fixed_len", c_i32),
+    ("out", c_vp), ("out_stride_b", c_i64), ("out_stride_h", c_i64), ("q_rot_out", c_vp),
+    ("scale", c_f32), ("rope_theta", c_f32), ("rotary_dim", c_i32), ("advance", c_i32), ("split", c_i32),
+    ("workspace", c_vp), ("workspace_bytes", c_sz),
+]
+
+
+class DecodeDescV1(ctypes.Structure):
+    """fcci_decode_desc as version 1 of the ABI laid it out (no trailing flags)."""
+    _fields_ = _DESC_V1_FIELDS
+
+
 class DecodeDesc(ctypes.Structure):
-    _fields_ = [
-        ("abi_version", c_i32), ("B", c_i32), ("Hq", c_i32), ("Hkv", c_i32), ("D", c_i32),
-        ("q", c_vp), ("q_stride_b", c_i64), ("q_stride_h", c_i64),
-        ("k_new", c_vp), ("k_new_stride_b", c_i64), ("k_new_stride_h", c_i64),
-        ("v_new", c_vp), ("v_new_stride_b", c_i64), ("v_new_stride_h", c_i64),
-        ("k_cache", c_vp), ("k_stride_b", c_i64), ("k_stride_h", c_i64), ("k_stride_t", c_i64),
-        ("v_cache", c_vp), ("v_stride_b", c_i64), ("v_stride_h", c_i64), ("v_stride_t", c_i64),
-        ("capacity", c_i32), ("cu_seqlens", c_vp), ("seq_lens", c_vp), ("fixed_len", c_i32),
-        ("out", c_vp), ("out_stride_b", c_i64), ("out_stride_h", c_i64), ("q_rot_out", c_vp),
-        ("scale", c_f32), ("rope_theta", c_f32), ("rotary_dim", c_i32), ("advance", c_i32), ("split", c_i32),
-        ("workspace", c_vp), ("workspace_bytes", c_sz),
-    ]
+    _fields_ = _DESC_V1_FIELDS + [("flags", ctypes.c_uint32)]
 
 
 def load(path: str = LIB_PATH):
@@ -47,7 +56,8 @@ def load(path: str = LIB_PATH):
 
 
 def batched_desc(q, k_cache, v_cache, out, *, k_new=None, v_new=None, seq_lens=None, fixed_len=0, scale=None,
-                 rope_theta=10000.0, rotary_dim=None, advance=False, split=True, workspace=None, q_rot_out=None):
+                 rope_theta=10000.0, rotary_dim=None, advance=False, split=True, workspace=None, q_rot_out=None,
+                 flags=0):
     """Descriptor for torch CUDA tensors: q [B,Hq,D], caches [B,Hkv,cap,D], out [B,Hq,D]."""
     B, Hq, D = q.shape
     Hkv, cap = k_cache.shape[1], k_cache.shape[2]
@@ -67,7 +77,7 @@ def batched_desc(q, k_cache, v_cache, out, *, k_new=None, v_new=None, seq_lens=N
     d.scale = scale if scale is not None else D ** -0.5
     d.rope_theta = rope_theta
     d.rotary_dim = (D if k_new is not None else 0) if rotary_dim is None else rotary_dim
-    d.advance, d.split = int(advance), int(split)
+    d.advance, d.split, d.flags = int(advance), int(split), int(flags)
     if workspace is not None:
         d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel()
     return d

@@ -90,3 +90,29 @@ def test_forward_checks_run_on_host():
     q = torch.zeros(4, 128, dtype=torch.float16)
     with pytest.raises(RuntimeError, match="must be CUDA"):
         pkg.attn_varlen.forward(q, q.view(4, 1, 128), q.view(4, 1, 128), 1, 1.0)
+
+
+def test_descriptor_layout_matches_header(tmp_path):
+    """The ctypes descriptors (version 2, and version 1 without the trailing flags) have
+    the C header's size and field offsets."""
+    import subprocess
+
+    import capi_ctypes as C
+
+    src = tmp_path / "layout.cpp"
+    src.write_text(
+        '#include <cstdio>\n#include <cstddef>\n#include "fcci_decode.h"\n'
+        "int main() { std::printf(\"%zu %zu %zu %d %u\\n\", sizeof(fcci_decode_desc),"
+        " offsetof(fcci_decode_desc, workspace_bytes), offsetof(fcci_decode_desc, flags),"
+        " FCCI_DECODE_ABI_VERSION, FCCI_DECODE_PREFETCH_KV); return 0; }\n")
+    exe = tmp_path / "layout"
+    cuda_inc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+    subprocess.run(["g++", "-I", os.path.join(ROOT, "include"), "-I", cuda_inc, str(src), "-o", str(exe)],
+                   check=True)
+    size, off_wsb, off_flags, abi, prefetch = subprocess.run([str(exe)], check=True, capture_output=True,
+                                                             text=True).stdout.split()
+    assert int(size) == ctypes.sizeof(C.DecodeDesc)
+    assert int(off_flags) == C.DecodeDesc.flags.offset
+    assert int(off_wsb) == C.DecodeDesc.workspace_bytes.offset == C.DecodeDescV1.workspace_bytes.offset
+    assert ctypes.sizeof(C.DecodeDescV1) <= int(off_flags)
+    assert int(abi) == C.ABI_VERSION and int(prefetch) == C.PREFETCH_KV

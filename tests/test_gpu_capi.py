@@ -77,3 +77,41 @@ def test_descriptor_errors_are_status_codes(lib):
     kc = torch.zeros(1, 8, 16, 128, dtype=torch.float16, device=DEV)
     d = C.batched_desc(q, kc, kc, q.clone(), fixed_len=4, split=True)  # split needs a workspace
     assert lib.fcci_decode_attention(ctypes.byref(d), None) == 3
+
+
+def test_descriptor_versions_and_flags(lib):
+    """A version-1 descriptor (no flags field) still works; FCCI_DECODE_PREFETCH_KV gives
+    the same bits; unknown flag bits are rejected with a status code."""
+    B, Hkv, G, D, cap = 4, 2, 8, 128, 900
+    lens = [3, 200, 880, 64]
+    q, kn, vn = randn_half((B, Hkv * G, D), 20), randn_half((B, Hkv, D), 21), randn_half((B, Hkv, D), 22)
+    kc, vc = randn_half((B, Hkv, cap, D), 23), randn_half((B, Hkv, cap, D), 24)
+    T = torch.tensor(lens, dtype=torch.int32)
+    nbytes = lib.fcci_decode_workspace_bytes(B, Hkv * G, Hkv, D, torch.cuda.current_device())
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.fcci_decode_workspace_init(ws.data_ptr(), nbytes, stream) == 0
+    outs = []
+    for version, flags in ((2, 0), (2, C.PREFETCH_KV), (1, 0)):
+        dk, dv, dT = kc.to(DEV), vc.to(DEV), T.to(DEV)
+        out = torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV)
+        d = C.batched_desc(q.to(DEV), dk, dv, out, k_new=kn.to(DEV), v_new=vn.to(DEV), seq_lens=dT, advance=True,
+                           workspace=ws, flags=flags)
+        if version == 1:
+            v1 = C.DecodeDescV1()
+            ctypes.memmove(ctypes.byref(v1), ctypes.byref(d), ctypes.sizeof(v1))
+            v1.abi_version = 1
+            rc = lib.fcci_decode_attention(ctypes.cast(ctypes.byref(v1), ctypes.POINTER(C.DecodeDesc)), stream)
+        else:
+            rc = lib.fcci_decode_attention(ctypes.byref(d), stream)
+        assert rc == 0, lib.fcci_last_error_string()
+        torch.cuda.synchronize()
+        assert dT.cpu().tolist() == [t + 1 for t in lens]
+        outs.append(out.cpu())
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    ma, rl = close(outs[0], O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn)["ctx"])
+    assert ma <= O.MAX_ABS_TOL and rl <= O.REL_L2_TOL, (ma, rl)
+    d = C.batched_desc(q.to(DEV), kc.to(DEV), vc.to(DEV), torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV),
+                       fixed_len=5, workspace=ws, flags=2)
+    assert lib.fcci_decode_attention(ctypes.byref(d), stream) == 1
+    assert b"flags" in lib.fcci_last_error_string()

@@ -323,3 +323,57 @@ def test_nan_past_end_does_not_leak(av):
     q, kn, vn, kc, vc, T, cu = make_case(3, 2, 8, 128, lens, 256, seed=1000)
     got = run_decode(av, q, kn, vn, kc, vc, T, cu)
     assert torch.isfinite(got["out"].float()).all()
+
+
+@pytest.mark.parametrize("lens_kind", ["uniform", "ragged"])
+def test_prefetch_kv_layer_chain(av, lens_kind):
+    """A chain of decode steps over four layers' arenas, as one token of a model runs them
+    (only the last advances seq_lens), captured in one graph. With prefetch_kv each launch
+    reads the lengths and its first cached K/V tiles before waiting for the previous
+    layer's launch. Outputs, arenas and lengths must be bit-identical to the same chain
+    without it, and each layer's output within tolerance of the oracle."""
+    L, B, Hkv, G, D = 4, 8, 2, 8, 128
+    lens = [1500] * B if lens_kind == "uniform" else [5, 64, 700, 1500, 129, 3000, 1, 2048]
+    cap = max(lens) + 4
+    cases = [make_case(B, Hkv, G, D, lens, cap, seed=1100 + 10 * l) for l in range(L)]
+    lens0 = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    results = {}
+    for prefetch in (False, True):
+        dq = [c[0].to(DEV) for c in cases]
+        dkn = [c[1].to(DEV) for c in cases]
+        dvn = [c[2].to(DEV) for c in cases]
+        dk = [c[3].to(DEV) for c in cases]
+        dv = [c[4].to(DEV) for c in cases]
+        dT = lens0.clone()
+        out = torch.full((L, B, Hkv * G, D), float("nan"), dtype=torch.float16, device=DEV)
+        ws = av.make_workspace(B, Hkv * G, Hkv, D)
+
+        def chain():
+            dT.copy_(lens0)
+            for l in range(L):
+                av.decode(dq[l], dk[l], dv[l], out[l], k_new=dkn[l], v_new=dvn[l], seq_lens=dT,
+                          advance=(l == L - 1), workspace=ws, split=True, prefetch_kv=prefetch)
+
+        chain()  # eager run (kernel attributes), then the same chain from a graph, twice
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                chain()
+        torch.cuda.synchronize()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        assert av.read_error(ws) == 0
+        results[prefetch] = (out.cpu(), [k.cpu() for k in dk], [v.cpu() for v in dv], dT.cpu())
+    plain, pre = results[False], results[True]
+    assert torch.equal(plain[0], pre[0])
+    # bit patterns: the rows past each sequence hold NaN
+    assert all(torch.equal(a.view(torch.int16), b.view(torch.int16)) for a, b in zip(plain[1] + plain[2],
+                                                                                      pre[1] + pre[2]))
+    assert pre[3].tolist() == [t + 1 for t in lens]
+    for l, (q, kn, vn, kc, vc, T, _) in enumerate(cases):
+        want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn)
+        assert_close(pre[0][l], want["ctx"], f"layer {l} prefetch_kv")
