@@ -325,7 +325,7 @@ def test_nan_past_end_does_not_leak(av):
     assert torch.isfinite(got["out"].float()).all()
 
 
-@pytest.mark.parametrize("lens_kind", ["uniform", "ragged"])
+@pytest.mark.parametrize("lens_kind", ["uniform", "ragged", "packed"])
 def test_prefetch_kv_layer_chain(av, lens_kind):
     """A chain of decode steps over four layers' arenas, as one token of a model runs them
     (only the last advances seq_lens), captured in one graph. With prefetch_kv each launch
@@ -335,8 +335,11 @@ def test_prefetch_kv_layer_chain(av, lens_kind):
     L, B, Hkv, G, D = 4, 8, 2, 8, 128
     lens = [1500] * B if lens_kind == "uniform" else [5, 64, 700, 1500, 129, 3000, 1, 2048]
     cap = max(lens) + 4
-    cases = [make_case(B, Hkv, G, D, lens, cap, seed=1100 + 10 * l) for l in range(L)]
+    packed = lens_kind == "packed"
+    cases = [make_case(B, Hkv, G, D, lens, None if packed else cap, seed=1100 + 10 * l, packed=packed)
+             for l in range(L)]
     lens0 = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    cu = cases[0][6].to(DEV) if packed else None
     results = {}
     for prefetch in (False, True):
         dq = [c[0].to(DEV) for c in cases]
@@ -351,7 +354,7 @@ def test_prefetch_kv_layer_chain(av, lens_kind):
         def chain():
             dT.copy_(lens0)
             for l in range(L):
-                av.decode(dq[l], dk[l], dv[l], out[l], k_new=dkn[l], v_new=dvn[l], seq_lens=dT,
+                av.decode(dq[l], dk[l], dv[l], out[l], k_new=dkn[l], v_new=dvn[l], seq_lens=dT, cu_seqlens=cu,
                           advance=(l == L - 1), workspace=ws, split=True, prefetch_kv=prefetch)
 
         chain()  # eager run (kernel attributes), then the same chain from a graph, twice
@@ -374,6 +377,6 @@ def test_prefetch_kv_layer_chain(av, lens_kind):
     assert all(torch.equal(a.view(torch.int16), b.view(torch.int16)) for a, b in zip(plain[1] + plain[2],
                                                                                       pre[1] + pre[2]))
     assert pre[3].tolist() == [t + 1 for t in lens]
-    for l, (q, kn, vn, kc, vc, T, _) in enumerate(cases):
-        want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn)
+    for l, (q, kn, vn, kc, vc, T, cu_l) in enumerate(cases):
+        want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn, cu_seqlens=cu_l)
         assert_close(pre[0][l], want["ctx"], f"layer {l} prefetch_kv")
