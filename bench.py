@@ -256,7 +256,11 @@ def run_step(st, gather=None):
 def ours(args):
     world, rank, local = dist_setup(args.gpus)
     w = workload(args.workload, args.layers)
-    st = build_state(w, world, rank)
+    if args.shard_of > 1 and world == 1:
+        # one GPU runs rank 0's share of an N-way partition (for profiling that shape alone)
+        st = build_state(w, args.shard_of, 0)
+    else:
+        st = build_state(w, world, rank)
     # each layer's launch may read its lengths and first K/V tiles while the previous
     # layer's launch drains: that launch writes only its own arena, ctx and workspace,
     # and only the last layer advances seq_lens (each step starts with a copy)
@@ -360,6 +364,7 @@ def ours(args):
             "workload": w["name"], "batch": w["B"], "q_heads": w["Hq"], "kv_heads": w["Hkv"], "head_dim": D,
             "kv_len": (w["lens"][0] if len(set(w["lens"])) == 1 else "seeded U[128,8192]"), "layers": L,
             "parallelism": ("kv-head shards x%d" % world) if not w["packed"] else ("sequence shards x%d" % world),
+            "shard_of": args.shard_of if world == 1 and args.shard_of > 1 else None,
             "gather_ctx": bool(args.gather_ctx and world > 1),
             "prefetch_kv": st["prefetch_kv"],
             "l2": "no flush: arena %.1f GB per GPU > 126 MB L2" % (st["arena"].k.numel() * 4 / 1e9),
@@ -1050,6 +1055,8 @@ def main():
                     choices=["gqa70b", "gqa70b_32k", "varlen7b", "mha7b", "prefill16", "llama7b"])
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--gather-ctx", action="store_true")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="with one GPU: run rank 0's share of an N-way partition of the workload (profiling)")
     ap.add_argument("--no-prefetch-kv", action="store_true",
                     help="decode launches read nothing before the previous launch finishes")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
