@@ -380,7 +380,7 @@ def ours(args):
         },
         "e2e": {"value": round(e2e_kv / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                "ms_per_step": round(e2e_ms / e2e["steps"], 4), "api": "attn_varlen.decode per layer, eager",
+                "ms_per_step": round(e2e_ms / e2e["steps"], 4), "api": e2e["api"],
                 "tokens_per_s": round(w["B"] * e2e["steps"] / (e2e_ms / 1e3), 1)},
         "gpu_launches": args.steps * L,
         "clocks": clocks,
@@ -392,14 +392,17 @@ def ours(args):
 
 def e2e_run(st, args, L):
     """Per step: pinned-host q/k_new/v_new -> device (copy stream, one layer ahead),
-    decode through attn_varlen.decode, ctx -> pinned host; timed with events."""
+    decode through attn_varlen.decode, ctx -> pinned host; timed with events. The step
+    (copies and launches) is captured once and replayed as a CUDA graph, as the
+    reference's capture/replay server runs its steps; eager calls when capture fails."""
     arena = st["arena"]
     hq = st["q"].cpu().pin_memory()
     hkn = st["kn"].cpu().pin_memory()
     hvn = st["vn"].cpu().pin_memory()
     hout = torch.empty(st["out"].shape, dtype=torch.float16).pin_memory()
     dq, dkn, dvn, dout = st["q"], st["kn"], st["vn"], st["out"]
-    comp = torch.cuda.current_stream()
+    comp = torch.cuda.Stream()
+    comp.wait_stream(torch.cuda.current_stream())
     copy_in = torch.cuda.Stream()
     copy_out = torch.cuda.Stream()
     steps = max(3, min(args.steps, 10))
@@ -427,16 +430,38 @@ def e2e_run(st, args, L):
                 hout[l].copy_(dout[l], non_blocking=True)
         comp.wait_stream(copy_out)
 
-    for _ in range(2):
-        one_step()
+    with torch.cuda.stream(comp):
+        for _ in range(2):
+            one_step()
     torch.cuda.synchronize()
+    graph, api = None, "CUDA graph of the step: host copies and attn_varlen.decode per layer"
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=comp):
+            one_step()
+        torch.cuda.synchronize()
+        graph = g
+    except Exception as exc:  # keep the e2e leg: eager calls, as a user without graphs makes them
+        torch.cuda.synchronize()
+        api = "attn_varlen.decode per layer, eager (graph capture failed: %s)" % str(exc).splitlines()[0][:80]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(comp)
-    for _ in range(steps):
-        one_step()
-    e1.record(comp)
+    with torch.cuda.stream(comp):
+        if graph is not None:
+            graph.replay()
+        else:
+            one_step()
+        e0.record(comp)
+        for _ in range(steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                one_step()
+        e1.record(comp)
     torch.cuda.synchronize()
-    return {"ms": e0.elapsed_time(e1), "steps": steps, "h2d": h2d, "d2h": d2h}
+    got = hout.to(torch.float32)
+    if not torch.equal(hout[-1], st["out"][-1].cpu()) or not torch.isfinite(got).all():
+        raise SystemExit("e2e: the ctx copied to the host differs from the device result")
+    return {"ms": e0.elapsed_time(e1), "steps": steps, "h2d": h2d, "d2h": d2h, "api": api}
 
 
 # ---------------------------------------------------------------- CPU oracle baseline
