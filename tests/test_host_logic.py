@@ -179,3 +179,22 @@ def test_partition_by_cost_prefill():
     parts = sharding.partition_by_cost([L * (L + 1) / 2 for L in lens], 2)
     assert sorted(i for p in parts for i in p) == list(range(5))
     assert 1 in parts[0]  # the longest goes first to rank 0
+
+
+def test_bench_algorithmic_work_per_launch():
+    """The algorithmic bytes and flops that bench.py divides by the measured launch time:
+    K+V of every attended key plus q, ctx and the new rows (decode), and the causal QK^T + PV
+    flops (prefill), on the bench workloads and on one rank's share of the 8-way kv-head shards."""
+    import bench
+    from fully_custom_cuda_inference_lamma2_b200.sharding import partition_kv_heads
+
+    w = bench.workload("gqa70b", None)
+    lens1 = [t + 1 for t in w["lens"]]
+    assert bench.algorithmic_bytes(w["B"], w["Hq"], w["Hkv"], w["D"], lens1) == 538_312_704
+    assert bench.kv_read_bytes(w["Hkv"], w["D"], lens1) == 32 * 4097 * 8 * 128 * 4
+    kv_lo, kv_hi, q_lo, q_hi = partition_kv_heads(w["Hkv"], w["Hq"], 8, 0)
+    assert (kv_hi - kv_lo, q_hi - q_lo) == (1, 8)
+    assert bench.algorithmic_bytes(w["B"], 8, 1, w["D"], lens1) == 67_289_088
+    p = bench.prefill_workload("prefill16", None)
+    assert sum(p["lens"]) == 39_876
+    assert bench.prefill_flops(p["Hq"], p["D"], p["lens"]) == 937_470_803_968
