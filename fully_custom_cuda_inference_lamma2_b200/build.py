@@ -64,13 +64,14 @@ def build_library(force: bool = False) -> str:
     deps = srcs + [os.path.join(CSRC, h) for h in LIB_HEADERS] + _common_headers()
     if not force and _newer(LIB, deps):
         return LIB
-    objs = []
+    from concurrent.futures import ThreadPoolExecutor
+
     with tempfile.TemporaryDirectory() as tmp:
-        for s in srcs:
-            o = os.path.join(tmp, os.path.basename(s) + ".o")
-            _run([NVCC, *GENCODE, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", INCLUDE,
-                  "-I", CSRC, "-c", s, "-o", o])
-            objs.append(o)
+        objs = [os.path.join(tmp, os.path.basename(s) + ".o") for s in srcs]
+        cmds = [[NVCC, *GENCODE, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", INCLUDE, "-I", CSRC,
+                 "-c", s, "-o", o] for s, o in zip(srcs, objs)]
+        with ThreadPoolExecutor(max_workers=min(len(cmds), os.cpu_count() or 1)) as pool:
+            list(pool.map(_run, cmds))
         tmp_lib = os.path.join(tmp, "libfcci_decode.so")
         _run([NVCC, *GENCODE, "-shared", "-Xcompiler", "-fPIC", *objs, "-o", tmp_lib, "-lcublas"])
         shutil.move(tmp_lib, LIB)

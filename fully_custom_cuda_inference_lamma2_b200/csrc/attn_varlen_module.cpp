@@ -44,7 +44,7 @@ void run_forward(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tenso
     if (workspace.has_value() && workspace->defined()) {
         ws = *workspace;
     } else if (may_allocate && seq_len > 256) {
-        ws = make_workspace(1, H, H, D, q.device());
+        ws = cached_workspace(1, H, H, D, q.device());
     }
     if (ws.defined()) {
         bind_workspace(d, ws);
@@ -184,7 +184,7 @@ void decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor out
     d.advance = advance ? 1 : 0;
     at::Tensor ws;
     if (workspace.has_value() && workspace->defined()) ws = *workspace;
-    else if (split || advance) ws = make_workspace(B, Hq, Hkv, D, q.device());
+    else if (split || advance) ws = cached_workspace(B, Hq, Hkv, D, q.device());
     if (ws.defined()) bind_workspace(d, ws);
     d.split = split ? 1 : 0;
     d.flags = prefetch_kv ? FCCI_DECODE_PREFETCH_KV : 0u;
@@ -443,6 +443,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         },
         py::arg("workspace"), py::arg("clear") = true);
     m.def("launch_count", []() { return (int64_t)fcci_launch_count(); });
+    m.def("clear_workspace_cache", &clear_workspace_cache,
+          "Drop the workspaces kept for calls made without one (forward, capture_decode with q); "
+          "needed only after a device timeout");
     m.def(
         "set_tuning", [](int64_t stages, int64_t ctas) { check_rc(fcci_decode_set_tuning((int)stages, (int)ctas), "set_tuning"); },
         py::arg("stages") = 0, py::arg("ctas_per_sm") = 0);

@@ -6,6 +6,9 @@
 #include <torch/extension.h>
 
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "fcci_decode.h"
 
@@ -59,6 +62,55 @@ inline at::Tensor make_workspace(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, 
     TORCH_CHECK(bytes > 0, "fcci_decode_workspace_bytes: invalid shape");
     at::Tensor ws = at::empty({(int64_t)bytes}, at::TensorOptions().dtype(at::kByte).device(dev));
     check_rc(fcci_decode_workspace_init(ws.data_ptr(), bytes, current_stream()), "fcci_decode_workspace_init");
+    return ws;
+}
+
+// Workspace for calls that were not given one (the reference-shaped `forward` and
+// `capture_decode(..., q=...)`): one zeroed buffer per (device, stream, shape), made
+// on first use and kept for the process, so that repeated calls neither allocate nor
+// launch a memset. Calls on one stream run in order, which is what sharing a
+// workspace needs; calls on another stream get their own. While the stream is being
+// captured a fresh workspace is made instead (from the graph's memory pool, zeroed
+// inside the graph), as a per-call allocation was before. The counters in a
+// workspace return to zero after every call; a call that timed out on the device
+// (FCCI_DEV_ERR_TIMEOUT) may leave them mid-count, and clear_workspace_cache() then
+// drops every cached buffer so that the next calls start from fresh zeroed ones.
+struct WorkspaceKey {
+    int dev;
+    uintptr_t stream;
+    int64_t B, Hq, Hkv, D;
+    bool operator<(const WorkspaceKey& o) const {
+        return std::tie(dev, stream, B, Hq, Hkv, D) < std::tie(o.dev, o.stream, o.B, o.Hq, o.Hkv, o.D);
+    }
+};
+
+inline std::mutex& workspace_cache_mutex() {
+    static std::mutex mu;
+    return mu;
+}
+
+inline std::map<WorkspaceKey, at::Tensor>& workspace_cache() {
+    static auto* cache = new std::map<WorkspaceKey, at::Tensor>();  // lives until exit
+    return *cache;
+}
+
+inline void clear_workspace_cache() {
+    std::lock_guard<std::mutex> lk(workspace_cache_mutex());
+    workspace_cache().clear();
+}
+
+inline at::Tensor cached_workspace(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, const at::Device& dev) {
+    const cudaStream_t s = current_stream();
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    TORCH_CHECK(cudaStreamIsCapturing(s, &cap) == cudaSuccess, "cudaStreamIsCapturing failed");
+    if (cap != cudaStreamCaptureStatusNone) return make_workspace(B, Hq, Hkv, D, dev);
+    const WorkspaceKey key{(int)dev.index(), reinterpret_cast<uintptr_t>(s), B, Hq, Hkv, D};
+    std::lock_guard<std::mutex> lk(workspace_cache_mutex());
+    auto& cache = workspace_cache();
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    at::Tensor ws = make_workspace(B, Hq, Hkv, D, dev);
+    if (cache.size() < 64) cache.emplace(key, ws);  // beyond 64 shapes: a workspace per call
     return ws;
 }
 

@@ -75,7 +75,7 @@ void attention_step(const at::Tensor& arena_k, const at::Tensor& arena_v, const 
     d.advance = advance ? 1 : 0;
     at::Tensor ws;
     if (workspace.has_value() && workspace->defined()) ws = *workspace;
-    else ws = make_workspace(1, Hq, Hkv, D, q.device());
+    else ws = cached_workspace(1, Hq, Hkv, D, q.device());
     bind_workspace(d, ws);
     d.split = 1;
     check_rc(fcci_decode_attention(&d, current_stream()), "capture_decode_step.attention_step");
@@ -272,6 +272,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def(
         "prepare_cublas", []() { prepare_cublas_handle(current_stream()); },
         "Prepare global cuBLAS handle on current stream (call before capture)");
+    m.def("clear_workspace_cache", &clear_workspace_cache,
+          "Drop the workspaces kept for attention steps called without one; needed only after a device timeout");
     m.def("rmsnorm", &rmsnorm, "Case4 fused RMSNorm (fp16)");
     m.def("rmsnorm_ptr", &rmsnorm_ptr, "Case4 fused RMSNorm with weight pointer (fp16)");
     m.def("swiglu", &swiglu, "Case4 SwiGLU (fp16)");

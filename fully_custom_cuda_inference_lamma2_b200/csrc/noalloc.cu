@@ -26,19 +26,31 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[FCCI_NOALLOC_SC
 
 // Device address of g_noalloc_scratch on device `dev` (the current device). In
 // host code the array's name is only a stand-in for the symbol, so the address
-// is looked up once per device with cudaGetSymbolAddress.
-static int noalloc_scratch(int dev, void** out) {
-    static std::once_flag once[128];
+// is looked up once per device with cudaGetSymbolAddress. A failed look-up is
+// not remembered: a later call (for example one made outside stream capture)
+// tries again. The look-up is refused while `stream` is capturing, because the
+// first use of the symbol on a device may have to load the module there.
+static int noalloc_scratch(int dev, cudaStream_t stream, void** out) {
+    static std::mutex mu;
     static void* addr[128];
-    static cudaError_t err[128];
     if (dev < 0 || dev >= 128) return set_status(FCCI_EINVAL, "fcci_decode_attention_noalloc: device index");
-    std::call_once(once[dev], [dev]() {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        cudaError_t e = cudaStreamIsCapturing(stream, &cap);
+        if (e != cudaSuccess) return set_cuda_status(e);
+        if (cap != cudaStreamCaptureStatusNone)
+            return set_status(FCCI_EINVAL,
+                              "fcci_decode_attention_noalloc: the first call on a device must come before any stream "
+                              "capture (it looks up the built-in scratch's device address)");
         void* p = nullptr;
-        err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_cuda_status(e);
+        }
         addr[dev] = p;
-        if (err[dev] != cudaSuccess) cudaGetLastError();
-    });
-    if (err[dev] != cudaSuccess) return set_cuda_status(err[dev]);
+    }
     *out = addr[dev];
     return FCCI_OK;
 }
@@ -61,7 +73,7 @@ extern "C" int fcci_decode_attention_noalloc(const fcci_decode_desc* desc, cudaS
         return fcci::set_status(FCCI_EWORKSPACE, msg);
     }
     void* scratch = nullptr;
-    int rc = fcci::noalloc_scratch(dev, &scratch);
+    int rc = fcci::noalloc_scratch(dev, stream, &scratch);
     if (rc) return rc;
     // the array keeps the previous call's contents: the counters and the error
     // word must start at zero
@@ -76,4 +88,15 @@ extern "C" int fcci_decode_attention_noalloc(const fcci_decode_desc* desc, cudaS
     d.workspace = scratch;
     d.workspace_bytes = FCCI_NOALLOC_SCRATCH_BYTES;
     return fcci_decode_attention(&d, stream);
+}
+
+extern "C" int fcci_decode_noalloc_read_error(uint32_t* flags, int clear, cudaStream_t stream) {
+    if (!flags) return fcci::set_status(FCCI_EINVAL, "fcci_decode_noalloc_read_error: flags is NULL");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fcci::set_cuda_status(e);
+    void* scratch = nullptr;
+    int rc = fcci::noalloc_scratch(dev, stream, &scratch);
+    if (rc) return rc;
+    return fcci_decode_read_error(scratch, flags, clear, stream);
 }

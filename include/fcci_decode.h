@@ -159,13 +159,22 @@ int fcci_decode_attention(const fcci_decode_desc* desc, cudaStream_t stream);
  * (see fcci_decode_workspace_bytes) are rejected with FCCI_EWORKSPACE and a
  * message. The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress, with that device current); make that first call before
- * any stream capture. Each call zeroes the array's counters and error word on
- * `stream` first. All calls share the one array: calls that overlap on the GPU
- * (other streams, other threads) race and must be serialised by the caller.
- * Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+ * any stream capture: a first call on a capturing stream is refused with
+ * FCCI_EINVAL, and a later call outside capture does the look-up. Each call
+ * zeroes the array's counters and error word on `stream` first. All calls share
+ * the one array: calls that overlap on the GPU (other streams, other threads)
+ * race and must be serialised by the caller. Nothing here calls cudaMalloc,
+ * cudaFree or an allocating library routine.
  */
 #define FCCI_NOALLOC_SCRATCH_BYTES (8u << 20)
 int fcci_decode_attention_noalloc(const fcci_decode_desc* desc, cudaStream_t stream);
+
+/* Device error word of the built-in scratch (FCCI_DEV_ERR_* bits of the last
+ * fcci_decode_attention_noalloc call on this device), as fcci_decode_read_error
+ * reads a caller workspace: synchronises `stream`, clears the word when clear != 0.
+ * Read it after a call and before the next one, which zeroes the word again.
+ * No counterpart in the reference; allocates nothing. */
+int fcci_decode_noalloc_read_error(uint32_t* flags, int clear, cudaStream_t stream);
 
 /* RoPE(q, k_new) at T_b and append of (k_rot, v_new) at T_b; no attention.
  * Same descriptor; out/scale/workspace/split are ignored; q_rot_out receives

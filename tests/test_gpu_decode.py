@@ -98,6 +98,41 @@ def test_forward_out_no_alloc_with_workspace(av):
     assert_close(out, O.attn_varlen_forward(q.cpu(), k.cpu(), v.cpu(), T, 0.0883883), "forward_out")
 
 
+def test_repeated_reference_calls_neither_allocate_nor_memset(av):
+    """forward() past 256 keys and capture_decode(..., q=...) without a workspace reuse one
+    zeroed workspace per (device, stream, shape): after the first call, further calls
+    change torch.cuda.memory_allocated() by the returned ctx alone and issue no memset."""
+    import fully_custom_cuda_inference_lamma2_b200 as pkg
+
+    H, D, T = 32, 128, 2000
+    q, k, v = randn_half((H, D), 13).to(DEV), randn_half((H, T, D), 14).to(DEV), randn_half((H, T, D), 15).to(DEV)
+    first = av.forward(q, k, v, T, 0.0883883)
+    ak = randn_half((1, 1, H, 600, D), 16).to(DEV)
+    avv = randn_half((1, 1, H, 600, D), 17).to(DEV)
+    sl = torch.tensor([500], dtype=torch.int32, device=DEV)
+    z32 = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ctrl = torch.zeros(1, 1, dtype=torch.int64, device=DEV)
+    logits = torch.zeros(1, 8, device=DEV)
+    kn, vn, ctx = torch.zeros(H, D, dtype=torch.float16, device=DEV), torch.zeros_like(q), torch.empty_like(q)
+    cds = pkg.capture_decode_step
+    cds.capture_decode(ctrl, ak, avv, sl, z32, logits, q=q, k_new=kn, v_new=vn, ctx_out=ctx, advance=False)
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    kept = []
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(4):
+            kept.append(av.forward(q, k, v, T, 0.0883883))
+            cds.capture_decode(ctrl, ak, avv, sl, z32, logits, q=q, k_new=kn, v_new=vn, ctx_out=ctx, advance=False)
+        torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() - before == sum(t.numel() * 2 for t in kept)
+    names = [e.name for e in prof.events()]
+    assert any("decode_attn_kernel" in n for n in names), "profiler recorded no kernels"
+    assert not any("memset" in n.lower() for n in names), "a memset ran inside the repeated calls"
+    assert all(torch.equal(t, first) for t in kept)
+
+
 def test_forward_rejects_bad_inputs(av):
     q = torch.zeros(4, 128, dtype=torch.float16, device=DEV)
     k = torch.zeros(4, 10, 128, dtype=torch.float16, device=DEV)
