@@ -72,6 +72,13 @@ def workload(name: str, layers: int | None):
     return w
 
 
+def with_kv_len(w, kv_len):
+    """The workload with every sequence at kv_len cached keys (measurement sweeps)."""
+    if kv_len:
+        w = dict(w, lens=[kv_len] * w["B"], packed=False)
+    return w
+
+
 def algorithmic_bytes(B, Hq, Hkv, D, lens_plus1, append=True):
     """Bytes one launch must move: K+V of the attended keys, q in, ctx out, new rows in and out."""
     kv = sum(lens_plus1) * Hkv * D * 2 * 2
@@ -386,7 +393,7 @@ def prefill_subrecord(local):
 
 def ours(args):
     world, rank, local = dist_setup(args.gpus)
-    w = workload(args.workload, args.layers)
+    w = with_kv_len(workload(args.workload, args.layers), args.kv_len)
     if args.shard_of > 1 and world == 1:
         # one GPU runs rank 0's share of an N-way partition (for profiling that shape alone)
         st = build_state(w, args.shard_of, 0)
@@ -454,15 +461,21 @@ def ours(args):
         ok_all = bool(t.item() > 0.5)
 
     # ---- e2e through the public API with host buffers (pinned), copies overlapped per layer
-    e2e = e2e_run(st, args, L)
-    e2e_ms = max_over_ranks(e2e["ms"], world)
-    e2e_kv = per_step_kv * e2e["steps"]
-    if world > 1:
-        import torch.distributed as dist
+    e2e_line = None
+    if not args.no_e2e:
+        e2e = e2e_run(st, args, L)
+        e2e_ms = max_over_ranks(e2e["ms"], world)
+        e2e_kv = per_step_kv * e2e["steps"]
+        if world > 1:
+            import torch.distributed as dist
 
-        t = torch.tensor([float(e2e_kv)], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t)
-        e2e_kv = float(t.item())
+            t = torch.tensor([float(e2e_kv)], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t)
+            e2e_kv = float(t.item())
+        e2e_line = {"value": round(e2e_kv / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                    "ms_per_step": round(e2e_ms / e2e["steps"], 4), "api": e2e["api"],
+                    "tokens_per_s": round(w["B"] * e2e["steps"] / (e2e_ms / 1e3), 1)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -522,6 +535,7 @@ def ours(args):
             "shard_of": args.shard_of if world == 1 and args.shard_of > 1 else None,
             "gather_ctx": bool(args.gather_ctx and world > 1),
             "prefetch_kv": not args.no_prefetch_kv,
+            "max_cluster": args.max_cluster or "auto",
             "l2": "no flush: arena %.1f GB per GPU > 126 MB L2" % arena_gb,
         },
         "tokens_per_s": round(tokens_per_s, 1),
@@ -534,10 +548,7 @@ def ours(args):
             "kernel": "decode_attn_kernel<128,1>", "algorithmic_bytes_per_launch": per_launch_alg,
             "avg_launch_ms": round(kernel_ms, 5),
         },
-        "e2e": {"value": round(e2e_kv / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
-                "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                "ms_per_step": round(e2e_ms / e2e["steps"], 4), "api": e2e["api"],
-                "tokens_per_s": round(w["B"] * e2e["steps"] / (e2e_ms / 1e3), 1)},
+        "e2e": e2e_line,
         "gpu_launches": args.steps * L,
         "clocks": clocks,
         "checked": checked,
@@ -1229,11 +1240,19 @@ def main():
                     help="decode launches read nothing before the previous launch finishes")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--max-cluster", type=int, default=0,
+                    help="largest thread-block cluster of the split decode launch (0 automatic, 1 none)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (A/B measurements)")
+    ap.add_argument("--kv-len", type=int, default=0, help="decode workloads: every sequence at this many keys")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="skip the per-configuration records (gqa70b_32k, varlen7b, mha7b, prefill16) of the default run")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.max_cluster and args.impl == "ours":
+        import fully_custom_cuda_inference_lamma2_b200 as fcci
+
+        fcci.attn_varlen.set_tuning(max_cluster=args.max_cluster)
     if args.workload == "llama7b":
         (llama_reference if args.impl == "reference" else llama_ours)(args)
     elif args.workload == "prefill16":

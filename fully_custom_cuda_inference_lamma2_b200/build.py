@@ -27,7 +27,7 @@ NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 LIB = os.path.join(PKG, "libfcci_decode.so")
-LIB_SOURCES = ["decode_attn.cu", "capi.cu", "compat.cu", "noalloc.cu", "prefill_attn.cu", "gemv.cu"]
+LIB_SOURCES = ["decode_attn.cu", "capi.cu", "compat.cu", "noalloc.cu", "prefill_attn.cu", "gemv.cu", "step.cu"]
 LIB_HEADERS = ["ptx.cuh", "tcgen05.cuh", "fcci_internal.h"]
 MODULES = {
     "attn_varlen": "attn_varlen_module.cpp",

@@ -447,6 +447,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "Drop the workspaces kept for calls made without one (forward, capture_decode with q); "
           "needed only after a device timeout");
     m.def(
-        "set_tuning", [](int64_t stages, int64_t ctas) { check_rc(fcci_decode_set_tuning((int)stages, (int)ctas), "set_tuning"); },
-        py::arg("stages") = 0, py::arg("ctas_per_sm") = 0);
+        "set_tuning",
+        [](int64_t stages, int64_t ctas, int64_t max_cluster) {
+            check_rc(fcci_decode_set_tuning((int)stages, (int)ctas), "set_tuning");
+            check_rc(fcci_decode_set_cluster_limit((int)max_cluster), "set_tuning");
+        },
+        "Measurement hook: pipeline stages, CTAs per SM and the largest cluster of the split mode (0 = automatic, "
+        "max_cluster 1 = no clusters)",
+        py::arg("stages") = 0, py::arg("ctas_per_sm") = 0, py::arg("max_cluster") = 0);
 }

@@ -113,6 +113,13 @@ int fcci_decode_set_tuning(int stages, int ctas_per_sm) {
     return fcci::set_status(FCCI_OK, nullptr);
 }
 
+int fcci_decode_set_cluster_limit(int max_cluster) {
+    if (max_cluster < 0 || max_cluster > 16)
+        return fcci::set_status(FCCI_EINVAL, "fcci_decode_set_cluster_limit: out of range (0..16)");
+    fcci::tuning().max_cluster = max_cluster;
+    return fcci::set_status(FCCI_OK, nullptr);
+}
+
 int fcci_last_status(void) { return fcci::t_status; }
 
 const char* fcci_last_error_string(void) { return fcci::t_msg; }

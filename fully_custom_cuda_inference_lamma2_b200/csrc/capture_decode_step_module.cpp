@@ -2,6 +2,10 @@
 // (custom_kernels/capture_decode_step.cpp:61-325) with the decode-attention step
 // added to capture_decode / capture_decode_ext as optional keyword arguments.
 // Existing 6-argument and 20-argument calls behave as in the reference.
+#include <pybind11/stl.h>
+
+#include <vector>
+
 #include "binding_common.h"
 #include "fcci_compat.h"
 
@@ -112,6 +116,94 @@ void capture_decode(at::Tensor ctrl_input, at::Tensor arena_k, at::Tensor arena_
     check_rc(fcci_last_status(), "capture_decode");
 }
 
+// Per-layer weights of the whole step, named as the keys of the reference's
+// weight_loader.load_and_pack dictionary (custom_kernels/weight_loader.py:367-393).
+struct LayerWeights {
+    std::vector<uint64_t> qkv_ptrs, o_ptrs, mlp_gate_ptrs, mlp_up_ptrs, mlp_down_ptrs, rms_in_ptrs, rms_post_ptrs;
+    uint64_t emb_ptr = 0;
+    bool given() const { return !qkv_ptrs.empty(); }
+};
+
+// The whole token step behind capture_decode_ext (fcci_llama_decode_step): the token
+// from ctrl_input, the residual in mlp_out_s, ctx in x_norm_s, SwiGLU output in act_s,
+// q/k/v in qkv_s, fp32 logits in logits_out; seq_len_dev advances by one.
+void full_step(const at::Tensor& ctrl_input, const at::Tensor& arena_k, const at::Tensor& arena_v,
+               const at::Tensor& seq_len_dev, const at::Tensor& logits_out, const at::Tensor& x_norm_s,
+               const at::Tensor& act_s, const at::Tensor& mlp_out_s, uint64_t rms_final_w, uint64_t w_vocab,
+               int64_t I, double rms_eps, const LayerWeights& w, const c10::optional<at::Tensor>& qkv_s,
+               int64_t q_heads, const c10::optional<at::Tensor>& workspace, double rope_theta, int64_t rotary_dim) {
+    check_arena(arena_k, arena_v);
+    TORCH_CHECK(arena_k.size(1) == 1, "arena batch dimension must be 1");
+    TORCH_CHECK(arena_k.is_contiguous() && arena_v.is_contiguous(), "arena must be contiguous");
+    const int64_t L = arena_k.size(0), Hkv = arena_k.size(2), max_len = arena_k.size(3), D = arena_k.size(4);
+    const int64_t Hq = q_heads > 0 ? q_heads : Hkv;
+    const int64_t H = mlp_out_s.numel(), V = logits_out.size(1);
+    TORCH_CHECK(ctrl_input.scalar_type() == at::kLong && ctrl_input.numel() >= 1, "ctrl_input must hold one int64");
+    check_int32_cuda(seq_len_dev, "seq_len_dev");
+    TORCH_CHECK(logits_out.scalar_type() == at::kFloat && logits_out.dim() == 2 && logits_out.is_contiguous(),
+                "logits_out must be a contiguous fp32 [1, vocab]");
+    TORCH_CHECK(Hq % Hkv == 0, "q_heads must be a multiple of the arena's kv heads");
+    TORCH_CHECK(given(qkv_s), "the whole step needs qkv_s ((q_heads + 2 kv_heads) * head_dim fp16)");
+    check_rows(*qkv_s, (Hq + 2 * Hkv) * D, "qkv_s");
+    check_rows(x_norm_s, Hq * D, "x_norm_s (holds ctx)");
+    check_rows(act_s, I, "act_s");
+    check_rows(mlp_out_s, H, "mlp_out_s (holds the residual)");
+    auto n_ok = [&](const std::vector<uint64_t>& v) { return (int64_t)v.size() == L; };
+    TORCH_CHECK(n_ok(w.qkv_ptrs) && n_ok(w.o_ptrs) && n_ok(w.mlp_gate_ptrs) && n_ok(w.mlp_up_ptrs) &&
+                    n_ok(w.mlp_down_ptrs) && n_ok(w.rms_in_ptrs) && n_ok(w.rms_post_ptrs),
+                "every per-layer pointer list needs one entry per arena layer (", L, ")");
+    TORCH_CHECK(w.emb_ptr != 0 && rms_final_w != 0, "the whole step needs emb_ptr and rms_final_w");
+    std::vector<const void*> qkv(L), o(L), gate(L), up(L), down(L), rin(L), rpost(L);
+    for (int64_t l = 0; l < L; ++l) {
+        qkv[l] = reinterpret_cast<const void*>(w.qkv_ptrs[l]);
+        o[l] = reinterpret_cast<const void*>(w.o_ptrs[l]);
+        gate[l] = reinterpret_cast<const void*>(w.mlp_gate_ptrs[l]);
+        up[l] = reinterpret_cast<const void*>(w.mlp_up_ptrs[l]);
+        down[l] = reinterpret_cast<const void*>(w.mlp_down_ptrs[l]);
+        rin[l] = reinterpret_cast<const void*>(w.rms_in_ptrs[l]);
+        rpost[l] = reinterpret_cast<const void*>(w.rms_post_ptrs[l]);
+    }
+    at::Tensor ws = given(workspace) ? *workspace : cached_workspace(1, Hq, Hkv, D, arena_k.device());
+    TORCH_CHECK(ws.is_cuda() && ws.scalar_type() == at::kByte && ws.is_contiguous(),
+                "workspace must be a contiguous uint8 CUDA tensor from attn_varlen.make_workspace()");
+    fcci_llama_step_desc d;
+    std::memset(&d, 0, sizeof(d));
+    d.abi_version = FCCI_LLAMA_STEP_ABI_VERSION;
+    d.layers = (int32_t)L;
+    d.hidden = (int32_t)H;
+    d.q_heads = (int32_t)Hq;
+    d.kv_heads = (int32_t)Hkv;
+    d.head_dim = (int32_t)D;
+    d.intermediate = (int32_t)I;
+    d.vocab = (int32_t)V;
+    d.rms_eps = (float)rms_eps;
+    d.rope_theta = (float)rope_theta;
+    d.rotary_dim = (int32_t)rotary_dim;
+    d.token = ctrl_input.data_ptr<int64_t>();
+    d.embed = reinterpret_cast<const void*>(w.emb_ptr);
+    d.w_qkv = qkv.data();
+    d.w_o = o.data();
+    d.w_gate = gate.data();
+    d.w_up = up.data();
+    d.w_down = down.data();
+    d.rms_in = rin.data();
+    d.rms_post = rpost.data();
+    d.rms_final = reinterpret_cast<const void*>(rms_final_w);
+    d.lm_head = reinterpret_cast<const void*>(w_vocab);
+    d.arena_k = arena_k.data_ptr();
+    d.arena_v = arena_v.data_ptr();
+    d.max_len = (int32_t)max_len;
+    d.seq_len = seq_len_dev.data_ptr<int32_t>();
+    d.x = mlp_out_s.data_ptr();
+    d.qkv = qkv_s->data_ptr();
+    d.ctx = x_norm_s.data_ptr();
+    d.act = act_s.data_ptr();
+    d.logits = logits_out.data_ptr<float>();
+    d.workspace = ws.data_ptr();
+    d.workspace_bytes = (size_t)ws.numel();
+    check_rc(fcci_llama_decode_step(&d, current_stream()), "capture_decode_ext (whole step)");
+}
+
 void capture_decode_ext(at::Tensor ctrl_input, at::Tensor arena_k, at::Tensor arena_v, at::Tensor seq_len_dev,
                         at::Tensor pos_dev, at::Tensor logits_out, at::Tensor x_norm_s, at::Tensor gate_out_s,
                         at::Tensor up_out_s, at::Tensor act_s, at::Tensor mlp_out_s, uint64_t rms_in_w,
@@ -119,7 +211,8 @@ void capture_decode_ext(at::Tensor ctrl_input, at::Tensor arena_k, at::Tensor ar
                         uint64_t w_vocab, int64_t I, double rms_eps, c10::optional<at::Tensor> q,
                         c10::optional<at::Tensor> k_new, c10::optional<at::Tensor> v_new,
                         c10::optional<at::Tensor> ctx_out, int64_t layer, c10::optional<at::Tensor> workspace,
-                        double scale, double rope_theta, int64_t rotary_dim, c10::optional<at::Tensor> q_rot_out) {
+                        double scale, double rope_theta, int64_t rotary_dim, c10::optional<at::Tensor> q_rot_out,
+                        const LayerWeights& lw, c10::optional<at::Tensor> qkv_s, int64_t q_heads) {
     TORCH_CHECK(ctrl_input.is_cuda() && arena_k.is_cuda() && arena_v.is_cuda() && seq_len_dev.is_cuda() &&
                     pos_dev.is_cuda() && logits_out.is_cuda(),
                 "all tensors must be CUDA");
@@ -131,6 +224,12 @@ void capture_decode_ext(at::Tensor ctrl_input, at::Tensor arena_k, at::Tensor ar
                     mlp_out_s.scalar_type() == at::kHalf,
                 "scratch must be fp16");
     c10::cuda::CUDAGuard guard(arena_k.device());
+    if (lw.given()) {
+        TORCH_CHECK(!given(q), "give either the per-layer weights (whole step) or q/k_new/v_new (one attention step)");
+        full_step(ctrl_input, arena_k, arena_v, seq_len_dev, logits_out, x_norm_s, act_s, mlp_out_s, rms_final_w,
+                  w_vocab, I, rms_eps, lw, qkv_s, q_heads, workspace, rope_theta, rotary_dim);
+        return;
+    }
     if (given(q)) {
         TORCH_CHECK(given(k_new) && given(v_new) && given(ctx_out), "the attention step needs q, k_new, v_new and ctx_out");
         // the _ext step bumps seq_len itself (below), so the attention step does not
@@ -260,15 +359,84 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("v_new") = py::none(), py::arg("ctx_out") = py::none(), py::arg("layer") = 0,
           py::arg("advance") = true, py::arg("workspace") = py::none(), py::arg("scale") = -1.0,
           py::arg("rope_theta") = 10000.0, py::arg("rotary_dim") = -1, py::arg("q_rot_out") = py::none());
-    m.def("capture_decode_ext", &capture_decode_ext, "Case4 custom capture/replay decode (extended args)",
-          py::arg("ctrl_input"), py::arg("arena_k"), py::arg("arena_v"), py::arg("seq_len_dev"), py::arg("pos_dev"),
-          py::arg("logits_out"), py::arg("x_norm_s"), py::arg("gate_out_s"), py::arg("up_out_s"), py::arg("act_s"),
-          py::arg("mlp_out_s"), py::arg("rms_in_w"), py::arg("rms_post_w"), py::arg("rms_final_w"),
-          py::arg("w_gate"), py::arg("w_up"), py::arg("w_down"), py::arg("w_vocab"), py::arg("I"),
-          py::arg("rms_eps"), py::arg("q") = py::none(), py::arg("k_new") = py::none(),
+    // 20 positional arguments as the reference module binds them (capture_decode_step.cpp:85-93), and 25 as the
+    // reference's server passes them (case4_graph_generator_server_ipc.py:2261, 2291, 2405, 2526: L, H, max_len,
+    // D and vocab before I and rms_eps, which this form checks against the tensors). Keyword arguments add the
+    // attention step of one layer (q, k_new, v_new, ctx_out, layer, ...) or, with the per-layer weight lists of
+    // weight_loader.load_and_pack (qkv_ptrs, o_ptrs, mlp_gate_ptrs, mlp_up_ptrs, mlp_down_ptrs, rms_in_ptrs,
+    // rms_post_ptrs, emb_ptr) and qkv_s, the whole token step of every layer.
+    auto ext20 = [](at::Tensor ctrl_input, at::Tensor arena_k, at::Tensor arena_v, at::Tensor seq_len_dev,
+                    at::Tensor pos_dev, at::Tensor logits_out, at::Tensor x_norm_s, at::Tensor gate_out_s,
+                    at::Tensor up_out_s, at::Tensor act_s, at::Tensor mlp_out_s, uint64_t rms_in_w,
+                    uint64_t rms_post_w, uint64_t rms_final_w, uint64_t w_gate, uint64_t w_up, uint64_t w_down,
+                    uint64_t w_vocab, int64_t I, double rms_eps, c10::optional<at::Tensor> q,
+                    c10::optional<at::Tensor> k_new, c10::optional<at::Tensor> v_new,
+                    c10::optional<at::Tensor> ctx_out, int64_t layer, c10::optional<at::Tensor> workspace,
+                    double scale, double rope_theta, int64_t rotary_dim, c10::optional<at::Tensor> q_rot_out,
+                    std::vector<uint64_t> qkv_ptrs, std::vector<uint64_t> o_ptrs,
+                    std::vector<uint64_t> mlp_gate_ptrs, std::vector<uint64_t> mlp_up_ptrs,
+                    std::vector<uint64_t> mlp_down_ptrs, std::vector<uint64_t> rms_in_ptrs,
+                    std::vector<uint64_t> rms_post_ptrs, uint64_t emb_ptr, c10::optional<at::Tensor> qkv_s,
+                    int64_t q_heads) {
+        LayerWeights lw{qkv_ptrs, o_ptrs, mlp_gate_ptrs, mlp_up_ptrs, mlp_down_ptrs, rms_in_ptrs, rms_post_ptrs,
+                        emb_ptr};
+        capture_decode_ext(ctrl_input, arena_k, arena_v, seq_len_dev, pos_dev, logits_out, x_norm_s, gate_out_s,
+                           up_out_s, act_s, mlp_out_s, rms_in_w, rms_post_w, rms_final_w, w_gate, w_up, w_down,
+                           w_vocab, I, rms_eps, q, k_new, v_new, ctx_out, layer, workspace, scale, rope_theta,
+                           rotary_dim, q_rot_out, lw, qkv_s, q_heads);
+    };
+    auto ext25 = [ext20](at::Tensor ctrl_input, at::Tensor arena_k, at::Tensor arena_v, at::Tensor seq_len_dev,
+                         at::Tensor pos_dev, at::Tensor logits_out, at::Tensor x_norm_s, at::Tensor gate_out_s,
+                         at::Tensor up_out_s, at::Tensor act_s, at::Tensor mlp_out_s, uint64_t rms_in_w,
+                         uint64_t rms_post_w, uint64_t rms_final_w, uint64_t w_gate, uint64_t w_up, uint64_t w_down,
+                         uint64_t w_vocab, int64_t L, int64_t H, int64_t max_len, int64_t D, int64_t vocab, int64_t I,
+                         double rms_eps, c10::optional<at::Tensor> q, c10::optional<at::Tensor> k_new,
+                         c10::optional<at::Tensor> v_new, c10::optional<at::Tensor> ctx_out, int64_t layer,
+                         c10::optional<at::Tensor> workspace, double scale, double rope_theta, int64_t rotary_dim,
+                         c10::optional<at::Tensor> q_rot_out, std::vector<uint64_t> qkv_ptrs,
+                         std::vector<uint64_t> o_ptrs, std::vector<uint64_t> mlp_gate_ptrs,
+                         std::vector<uint64_t> mlp_up_ptrs, std::vector<uint64_t> mlp_down_ptrs,
+                         std::vector<uint64_t> rms_in_ptrs, std::vector<uint64_t> rms_post_ptrs, uint64_t emb_ptr,
+                         c10::optional<at::Tensor> qkv_s, int64_t q_heads) {
+        TORCH_CHECK(arena_k.dim() == 5, "arena must be [L, 1, H, max_len, D]");
+        TORCH_CHECK(L == arena_k.size(0) && max_len == arena_k.size(3) && D == arena_k.size(4) &&
+                        vocab == logits_out.size(1),
+                    "capture_decode_ext: L, max_len, D and vocab must match the arena and logits_out");
+        TORCH_CHECK(H == arena_k.size(2) || H == mlp_out_s.numel(),
+                    "capture_decode_ext: H must be the arena's heads or the hidden size");
+        ext20(ctrl_input, arena_k, arena_v, seq_len_dev, pos_dev, logits_out, x_norm_s, gate_out_s, up_out_s, act_s,
+              mlp_out_s, rms_in_w, rms_post_w, rms_final_w, w_gate, w_up, w_down, w_vocab, I, rms_eps, q, k_new, v_new,
+              ctx_out, layer, workspace, scale, rope_theta, rotary_dim, q_rot_out, qkv_ptrs, o_ptrs, mlp_gate_ptrs,
+              mlp_up_ptrs, mlp_down_ptrs, rms_in_ptrs, rms_post_ptrs, emb_ptr, qkv_s, q_heads);
+    };
+    const char* ext_doc = "Case4 custom capture/replay decode (extended args)";
+    m.def("capture_decode_ext", ext20, ext_doc, py::arg("ctrl_input"), py::arg("arena_k"), py::arg("arena_v"),
+          py::arg("seq_len_dev"), py::arg("pos_dev"), py::arg("logits_out"), py::arg("x_norm_s"),
+          py::arg("gate_out_s"), py::arg("up_out_s"), py::arg("act_s"), py::arg("mlp_out_s"), py::arg("rms_in_w"),
+          py::arg("rms_post_w"), py::arg("rms_final_w"), py::arg("w_gate"), py::arg("w_up"), py::arg("w_down"),
+          py::arg("w_vocab"), py::arg("I"), py::arg("rms_eps"), py::arg("q") = py::none(),
+          py::arg("k_new") = py::none(), py::arg("v_new") = py::none(), py::arg("ctx_out") = py::none(),
+          py::arg("layer") = 0, py::arg("workspace") = py::none(), py::arg("scale") = -1.0,
+          py::arg("rope_theta") = 10000.0, py::arg("rotary_dim") = -1, py::arg("q_rot_out") = py::none(),
+          py::kw_only(), py::arg("qkv_ptrs") = std::vector<uint64_t>(), py::arg("o_ptrs") = std::vector<uint64_t>(),
+          py::arg("mlp_gate_ptrs") = std::vector<uint64_t>(), py::arg("mlp_up_ptrs") = std::vector<uint64_t>(),
+          py::arg("mlp_down_ptrs") = std::vector<uint64_t>(), py::arg("rms_in_ptrs") = std::vector<uint64_t>(),
+          py::arg("rms_post_ptrs") = std::vector<uint64_t>(), py::arg("emb_ptr") = 0,
+          py::arg("qkv_s") = py::none(), py::arg("q_heads") = -1);
+    m.def("capture_decode_ext", ext25, ext_doc, py::arg("ctrl_input"), py::arg("arena_k"), py::arg("arena_v"),
+          py::arg("seq_len_dev"), py::arg("pos_dev"), py::arg("logits_out"), py::arg("x_norm_s"),
+          py::arg("gate_out_s"), py::arg("up_out_s"), py::arg("act_s"), py::arg("mlp_out_s"), py::arg("rms_in_w"),
+          py::arg("rms_post_w"), py::arg("rms_final_w"), py::arg("w_gate"), py::arg("w_up"), py::arg("w_down"),
+          py::arg("w_vocab"), py::arg("L"), py::arg("H"), py::arg("max_len"), py::arg("D"), py::arg("vocab"),
+          py::arg("I"), py::arg("rms_eps"), py::arg("q") = py::none(), py::arg("k_new") = py::none(),
           py::arg("v_new") = py::none(), py::arg("ctx_out") = py::none(), py::arg("layer") = 0,
           py::arg("workspace") = py::none(), py::arg("scale") = -1.0, py::arg("rope_theta") = 10000.0,
-          py::arg("rotary_dim") = -1, py::arg("q_rot_out") = py::none());
+          py::arg("rotary_dim") = -1, py::arg("q_rot_out") = py::none(), py::kw_only(),
+          py::arg("qkv_ptrs") = std::vector<uint64_t>(), py::arg("o_ptrs") = std::vector<uint64_t>(),
+          py::arg("mlp_gate_ptrs") = std::vector<uint64_t>(), py::arg("mlp_up_ptrs") = std::vector<uint64_t>(),
+          py::arg("mlp_down_ptrs") = std::vector<uint64_t>(), py::arg("rms_in_ptrs") = std::vector<uint64_t>(),
+          py::arg("rms_post_ptrs") = std::vector<uint64_t>(), py::arg("emb_ptr") = 0,
+          py::arg("qkv_s") = py::none(), py::arg("q_heads") = -1);
     m.def(
         "prepare_cublas", []() { prepare_cublas_handle(current_stream()); },
         "Prepare global cuBLAS handle on current stream (call before capture)");

@@ -14,8 +14,14 @@
 // whatever the length mix. A pair lying inside one CTA's range is finished by
 // that CTA; a pair cut by CTA boundaries leaves one partial (o, lse) per piece
 // in slot (pair + cta) — unique because both cut sets are ordered — and the
-// last piece to finish (atomic counter, never waited on) merges them. In pair
-// mode there is one CTA per pair and no workspace.
+// last piece to finish (atomic counter, never waited on) merges them. When there
+// are few pairs (at most half as many as CTAs) the split grid is launched as
+// thread-block clusters of k CTAs, one cluster per pair: with uniform tile counts
+// each CTA of a cluster takes 1/k of its pair's tiles, keeps its (o, lse) piece
+// in shared memory, and after a cluster barrier each CTA merges a slice of the
+// outputs from all k pieces through distributed shared memory. No CTA ever waits
+// on another CTA's global counter. In pair mode there is one CTA per pair and no
+// workspace.
 //
 // Inside a CTA: warp 4 is the TMA producer (one thread), warps 0..3 consume.
 // A stage holds the K and V tiles of 64 keys (2 x 64 x D fp16), loaded as
@@ -38,7 +44,9 @@
 #include <string.h>
 
 #include <atomic>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "fcci_decode.h"
 #include "fcci_internal.h"
@@ -54,7 +62,7 @@ constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kBoxBytes = kGroupKeys * 128;  // 16 rows x 64 fp16
 constexpr int kHalfTileBytes = kTileKeys * 128;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any healthy wait
-constexpr int kCoopPieces = 6;  // pieces per pair from which the piece CTAs merge a slice each
+constexpr int kMaxCluster = 16;  // CTAs per cluster of a cluster launch (non-portable above 8)
 constexpr uint64_t kDrainLimitNs = 500000000ull;
 constexpr int kConsumerBar = 1;
 
@@ -83,6 +91,7 @@ struct Params {
     int32_t append;
     int32_t split;
     int32_t prefetch_kv;  // FCCI_DECODE_PREFETCH_KV: lengths and the first stages before griddepcontrol.wait
+    int32_t cluster_k;    // CTAs per cluster of a split launch in clusters of one pair each; 0 otherwise
     int32_t B, Hq, Hkv, G;
     int32_t stages;
     uint32_t* err;
@@ -169,7 +178,8 @@ struct Layout {
     static __host__ __device__ constexpr size_t stage_bytes() { return 2 * (size_t)KT; }
     static __host__ __device__ constexpr size_t fixed_bytes(int stages) {
         return (size_t)stages * stage_bytes() + sizeof(float) * RED +
-               sizeof(float) * kConsumerWarps * G8 * 2 + sizeof(__half) * G8 * QP + sizeof(float2) * (D / 2) +
+               sizeof(float) * kConsumerWarps * G8 * 2 + sizeof(float) * G8 * (D + 1) + sizeof(__half) * G8 * QP +
+               sizeof(float2) * (D / 2) +
                sizeof(uint64_t) * 2 * stages + sizeof(int) * 8;
     }
     static __host__ size_t smem_bytes(int stages, int B, bool split) {
@@ -198,7 +208,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     uint8_t* stages = sm;
     float* red_acc = reinterpret_cast<float*>(stages + (size_t)S * LY::stage_bytes());
     float* red_ml = red_acc + LY::RED;
-    __half* qrot = reinterpret_cast<__half*>(red_ml + kConsumerWarps * G8 * 2);
+    float* xo = red_ml + kConsumerWarps * G8 * 2;  // this CTA's normalised piece o [G8, D] (cluster merge)
+    float* xl = xo + G8 * D;                       // and its log2-sum-exp [G8]
+    __half* qrot = reinterpret_cast<__half*>(xl + G8);
     float2* rope_cs = reinterpret_cast<float2*>(qrot + G8 * QP);
     uint64_t* full = reinterpret_cast<uint64_t*>(rope_cs + D / 2);
     uint64_t* empty = full + S;
@@ -288,6 +300,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     long long t_begin = 0, t_end = 0, N = 0;
     int b0 = 0, h0 = 0, j0 = 0;
     long long C = gridDim.x;  // CTAs that take tiles: never more than there are tiles
+    const int ck = p.cluster_k;  // CTAs per cluster (cluster launch), else 0
+    bool cmode = false;          // one cluster per pair, the pair's tiles split over k_eff of its CTAs
+    int k_eff = 1;
     if (p.split) {
         N = tile_base[B];
         C = N < (long long)gridDim.x ? N : (long long)gridDim.x;
@@ -297,7 +312,21 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         // and when pairs are short, or many enough to fill half the grid, one CTA per
         // pair: no pieces and no merge, which cost more than the lost parallelism
         const long long P = (long long)B * Hkv;
-        if (uniform && P <= (long long)gridDim.x) {
+        if (ck > 1 && uniform && P * ck == (long long)gridDim.x) {
+            // cluster launch, uniform tile counts: cluster c serves pair c; CTA r of it takes
+            // the r-th of k_eff equal parts of the pair's tiles (k_eff <= tiles, so none is
+            // empty); CTAs r >= k_eff only join the cluster barriers
+            cmode = true;
+            const long long tp = N / P;
+            k_eff = (int)(tp < ck ? tp : ck);
+            const long long pr = blockIdx.x / ck;
+            const int r = (int)(blockIdx.x % ck);
+            C = P * k_eff;
+            if (r < k_eff) {
+                t_begin = pr * tp + r * tp / k_eff;
+                t_end = pr * tp + (r + 1) * tp / k_eff;
+            }
+        } else if (uniform && P <= (long long)gridDim.x) {
             const long long tp = N / P;
             if (tp <= kPairTiles || (2 * P >= (long long)gridDim.x && tp <= 4 * kPairTiles)) {
                 C = P;
@@ -313,7 +342,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 C = P * ((long long)gridDim.x / P);
             }
         }
-        if ((long long)blockIdx.x < C) {
+        if (!cmode && (long long)blockIdx.x < C) {
             t_begin = (long long)blockIdx.x * N / C;
             t_end = ((long long)blockIdx.x + 1) * N / C;
         }
@@ -664,18 +693,16 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 named_bar_sync(kConsumerBar, kConsumerThreads);
 
                 const int pidx = b * Hkv + h;
-                bool whole = true, coop = false;
+                bool whole = true;
                 int c0 = 0, c1 = 0;
-                if (p.split) {
+                if (cmode) {
+                    // the piece stays in this CTA's shared memory for the cluster merge
+                    whole = (k_eff == 1);
+                } else if (p.split) {
                     const long long pfirst = tile_base[b] + (long long)h * tiles;
                     c0 = cta_of_tile(pfirst, N, C);
                     c1 = cta_of_tile(pfirst + tiles - 1, N, C);
                     whole = (c0 == c1);
-                    // every piece of the pair ends its CTA's range (pair-aligned ranges): the
-                    // pieces' CTAs can wait for one another and merge a slice each, as no CTA
-                    // has a later segment that the wait would hold up. Taken from kCoopPieces
-                    // pieces up (measured: 9 pieces -9 % per launch, 4 even, 2 +5 %)
-                    coop = !whole && c1 - c0 + 1 >= kCoopPieces && (pfirst + tiles == ((long long)c1 + 1) * N / C);
                 }
                 const int slot = pidx + blockIdx.x;
                 __half* ob = p.out + (int64_t)b * p.o_sb;
@@ -699,6 +726,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     if (whole) {
                         *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) =
                             __floats2half2_rn(o0 * inv, o1 * inv);
+                    } else if (cmode) {
+                        *reinterpret_cast<float2*>(xo + hh * D + d) = make_float2(o0 * inv, o1 * inv);
+                        if (d == 0) xl[hh] = Ls > 0.f ? M + __log2f(Ls) : -INFINITY;
                     } else {
                         *reinterpret_cast<float2*>(p.part_o + ((size_t)slot * G + hh) * D + d) =
                             make_float2(o0 * inv, o1 * inv);
@@ -706,60 +736,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     }
                 }
                 named_bar_sync(kConsumerBar, kConsumerThreads);
-                if (coop) {
-                    // ---- all pieces of the pair arrive (counter to nparts), then each CTA
-                    //      merges its slice of the G x D outputs over every piece, in piece
-                    //      order with the running log-sum-exp of the single-merger path below
-                    //      (same arithmetic per element); the second round of increments
-                    //      (to 2 nparts) tells the last CTA to reset the counter
-                    const int nparts = c1 - c0 + 1;
-                    if (ctid == 0) {
-                        __threadfence();
-                        atomicAdd(&p.pair_cnt[pidx], 1u);
-                        volatile unsigned* cnt = &p.pair_cnt[pidx];
-                        int ok = 1;
-                        if (*cnt < (unsigned)nparts) {
-                            const uint64_t t0 = global_timer_ns();
-                            while (*cnt < (unsigned)nparts) {
-                                if (global_timer_ns() - t0 > kWaitLimitNs) {
-                                    ok = 0;
-                                    set_error(p, FCCI_DEV_ERR_TIMEOUT);
-                                    break;
-                                }
-                            }
-                        }
-                        __threadfence();
-                        misc[1] = ok;
-                    }
-                    named_bar_sync(kConsumerBar, kConsumerThreads);
-                    if (misc[1]) {
-                        const float* pl = p.part_lse + (size_t)(pidx + c0) * G;
-                        const float* po = p.part_o + (size_t)(pidx + c0) * G * D;
-                        const int E = G * D, r = (int)blockIdx.x - c0;
-                        const int lo = (int)((long long)r * E / nparts), hi = (int)((long long)(r + 1) * E / nparts);
-                        for (int e = lo + ctid; e < hi; e += kConsumerThreads) {
-                            const int hh = e / D;
-                            const int d = e - hh * D;
-                            float Mx = -INFINITY, Wt = 0.f, Ov = 0.f;
-                            for (int c = 0; c < nparts; ++c) {
-                                const float lse = __ldcg(pl + (size_t)c * G + hh);
-                                const float ov = __ldcg(po + (size_t)c * G * D + e);
-                                if (lse != -INFINITY) {
-                                    const float mn = fmaxf(Mx, lse);
-                                    const float a = ex2(Mx - mn), wgt = ex2(lse - mn);
-                                    Wt = Wt * a + wgt;
-                                    Ov = Ov * a + wgt * ov;
-                                    Mx = mn;
-                                }
-                            }
-                            const float inv = Wt > 0.f ? 1.f / Wt : 0.f;
-                            ob[(int64_t)(h * G + hh) * p.o_sh + d] = __float2half_rn(Ov * inv);
-                        }
-                    }
-                    named_bar_sync(kConsumerBar, kConsumerThreads);
-                    if (ctid == 0 && atomicAdd(&p.pair_cnt[pidx], 1u) == 2u * (unsigned)nparts - 1u)
-                        atomicExch(&p.pair_cnt[pidx], 0u);
-                } else if (!whole) {
+                if (!whole && !cmode) {
                     // ---- the last piece of a cut pair merges every piece's (o, lse).
                     //      The barrier above orders this CTA's piece stores before thread
                     //      0's fence and counter increment (release); the last arriver
@@ -846,6 +823,51 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
 
     __syncthreads();
+    if (ck > 1) {
+        // ---- cluster merge. Every CTA of the cluster executes both barriers, whatever its
+        //      range (idle CTAs and the non-uniform fallback included), so none waits for a
+        //      CTA that does not come. After the first, every piece is visible in its CTA's
+        //      shared memory; CTA r merges the r-th slice of the pair's G x D outputs over the
+        //      k_eff pieces, in piece order with a running log-sum-exp, reading them through
+        //      distributed shared memory. The second keeps every CTA (and so its shared memory)
+        //      alive until the others have read it.
+        cluster_sync_all();
+        const int r = (int)(blockIdx.x % ck);
+        if (cmode && k_eff > 1 && r < k_eff && warp < kConsumerWarps) {
+            const int pr = (int)(blockIdx.x / ck);
+            const int mb = pr / Hkv, mh = pr - mb * Hkv;
+            __half* obm = p.out + (int64_t)mb * p.o_sb + (int64_t)(mh * G) * p.o_sh;
+            const int E = G * D;
+            const int lo = (int)((long long)r * E / k_eff), hi = (int)((long long)(r + 1) * E / k_eff);
+            const uint32_t xo_s = smem_u32(xo), xl_s = smem_u32(xl);
+            for (int e = lo + tid; e < hi; e += kConsumerThreads) {
+                const int hh = e / D;
+                const int d = e - hh * D;
+                float lv[kMaxCluster], ov[kMaxCluster];
+#pragma unroll
+                for (int c = 0; c < kMaxCluster; ++c) {
+                    if (c < k_eff) {
+                        lv[c] = ld_cluster_f32(cluster_map(xl_s + 4u * hh, (uint32_t)c));
+                        ov[c] = ld_cluster_f32(cluster_map(xo_s + 4u * e, (uint32_t)c));
+                    }
+                }
+                float Mx = -INFINITY, Wt = 0.f, Ov = 0.f;
+#pragma unroll
+                for (int c = 0; c < kMaxCluster; ++c) {
+                    if (c < k_eff && lv[c] != -INFINITY) {
+                        const float mn = fmaxf(Mx, lv[c]);
+                        const float a = ex2(Mx - mn), wgt = ex2(lv[c] - mn);
+                        Wt = Wt * a + wgt;
+                        Ov = Ov * a + wgt * ov[c];
+                        Mx = mn;
+                    }
+                }
+                const float inv = Wt > 0.f ? 1.f / Wt : 0.f;
+                obm[(int64_t)hh * p.o_sh + d] = __float2half_rn(Ov * inv);
+            }
+        }
+        cluster_sync_all();
+    }
     // ---- device-side seq_len advance once every CTA has read the lengths
     if (p.advance) {
         if (tid == 0) {
@@ -1018,17 +1040,60 @@ WorkspaceLayout workspace_layout(int B, int Hq, int Hkv, int D, int grid) {
 
 int max_grid(int dev) { return device_sm_count(dev) * kMaxCtasPerSm; }
 
+// Can `clusters` clusters of k CTAs of this kernel (with `smem` bytes of dynamic shared
+// memory each) be resident on device `dev` at once? Answered by the occupancy API and
+// remembered per (device, k, shared memory).
 template <int D, int NB>
-static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mk64,
+static bool clusters_fit(int k, long long clusters, size_t smem, int dev, bool non_portable_ok) {
+    if (k > 8 && !non_portable_ok) return false;
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, size_t>, int> cache;
+    const auto key = std::make_tuple(dev, k, smem);
+    int n = -1;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) n = it->second;
+    }
+    if (n < 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(k * (clusters > 0 ? clusters : 1)));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute a[1];
+        a[0].id = cudaLaunchAttributeClusterDimension;
+        a[0].val.clusterDim.x = (unsigned)k;
+        a[0].val.clusterDim.y = 1;
+        a[0].val.clusterDim.z = 1;
+        cfg.attrs = a;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<D, NB>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        std::lock_guard<std::mutex> lk(mu);
+        cache[key] = n;
+    }
+    return (long long)n >= clusters;
+}
+
+template <int D, int NB>
+static int launch_decode_t(Params prm, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mk64,
                            const CUtensorMap& mv64, int grid, cudaStream_t st,
                            int dev) {
     using LY = Layout<D, NB>;
     static std::once_flag flags[128];
     static cudaError_t attr_err[128];
+    static bool non_portable[128];
     if (dev < 0 || dev >= 128) return FCCI_EINVAL;
     std::call_once(flags[dev], [&]() {
         attr_err[dev] = cudaFuncSetAttribute(decode_attn_kernel<D, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              227 * 1024);
+        // clusters of more than 8 CTAs need this opt-in; without it they are not used
+        non_portable[dev] =
+            cudaFuncSetAttribute(decode_attn_kernel<D, NB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+            cudaSuccess;
+        if (!non_portable[dev]) cudaGetLastError();
     });
     if (attr_err[dev] != cudaSuccess) return set_cuda_status(attr_err[dev]);
     const size_t smem = LY::smem_bytes(prm.stages, prm.B, prm.split != 0);
@@ -1055,8 +1120,27 @@ static int launch_decode_t(const Params& prm, const CUtensorMap& mk, const CUten
             occ_val[dev] = occ;
         }
         if (occ >= 1 && grid > device_sm_count(dev) * occ) grid = device_sm_count(dev) * occ;
+        // few (sequence, kv head) pairs: one cluster of k CTAs per pair, k as large as the
+        // resident grid allows (every cluster resident at once, so no second wave)
+        prm.cluster_k = 0;
+        const long long P = (long long)prm.B * prm.Hkv;
+        const int maxk = g_tuning.max_cluster > 0 ? g_tuning.max_cluster : kMaxCluster;
+        // a batched arena bounds every pair's tiles by its capacity: no cluster needs
+        // more CTAs than that (the packed layout gives no per-sequence bound here)
+        const long long cap_tiles = prm.cu_seqlens ? (long long)kMaxCluster : ((long long)prm.capacity + kTileKeys - 1) / kTileKeys;
+        if (maxk >= 2 && 2 * P <= (long long)grid && cap_tiles >= 2) {
+            long long k = (long long)grid / P;
+            if (k > maxk) k = maxk;
+            if (k > cap_tiles) k = cap_tiles;
+            while (k >= 2 && !clusters_fit<D, NB>((int)k, P, smem, dev, non_portable[dev])) --k;
+            if (k >= 2) {
+                prm.cluster_k = (int)k;
+                grid = (int)(P * k);
+            }
+        }
     }
-    return launch_pdl(decode_attn_kernel<D, NB>, dim3(grid), dim3(kThreads), smem, st, mk, mv, mk64, mv64, prm);
+    return launch_pdl_cluster(decode_attn_kernel<D, NB>, dim3(grid), dim3(kThreads), smem, st, prm.cluster_k, mk, mv,
+                              mk64, mv64, prm);
 }
 
 // Launch shape: persistent CTAs per SM and pipeline stages per CTA. Two CTAs

@@ -17,6 +17,7 @@ constexpr int kMaxCtasPerSm = 2;
 struct Tuning {
     int stages = 0;       // pipeline depth (64-key K+V tiles per CTA); 0 = automatic
     int ctas_per_sm = 0;  // persistent CTAs per SM in split mode; 0 = automatic
+    int max_cluster = 0;  // largest cluster of a split launch; 0 = automatic (16), 1 = no clusters
 };
 Tuning& tuning();
 
@@ -55,6 +56,45 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     count_launch();
     return set_cuda_status(e == cudaSuccess ? cudaGetLastError() : e);
 }
+// The same with `cluster` CTAs per thread-block cluster (1-D); cluster <= 1 launches
+// without clusters.
+template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       int cluster, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster > 1 ? (unsigned)cluster : 1u;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cluster > 1 ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    count_launch();
+    return set_cuda_status(e == cudaSuccess ? cudaGetLastError() : e);
+}
 int rope_append(const fcci_decode_desc* d, cudaStream_t stream);
+
+// The batch-1 projection of gemv.cu with two additions over fcci_gemv_desc: the up
+// rows of the SwiGLU mode as a separate matrix W2 (NULL: rows N..2N-1 of W), and mode
+// 3, which stores y in fp32 (the vocab projection's logits).
+struct GemvArgs {
+    const void* W;
+    const void* W2;
+    int64_t ld_w;
+    int32_t N, K;
+    const void* x;
+    const void* rms_w;
+    float eps;
+    void* out;
+    int32_t mode;
+};
+int gemv(const GemvArgs* d, cudaStream_t stream);
 
 }  // namespace fcci

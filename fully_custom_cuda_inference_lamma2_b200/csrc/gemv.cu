@@ -2,7 +2,9 @@
 //   y = W a                    with a = RMSNorm(x) * w_rms (prologue) or a = x
 //   out  = y                   (mode STORE)
 //   out += y                   (mode RESIDUAL: the residual stream update)
-//   out  = SiLU(y_g) * y_u     (mode SWIGLU: W holds the gate rows, then the up rows)
+//   out  = SiLU(y_g) * y_u     (mode SWIGLU: W holds the gate rows, then the up rows,
+//                               or the up rows are a second matrix W2)
+//   out  = y in fp32           (mode STORE_F32: the vocab projection's logits)
 // They replace, per layer of the reference's in-graph step
 // (custom_kernels/capture_decode_step_kernel.cu:137-274, capture_decode_step.cpp:176-310),
 // the RMSNorm kernel, the cuBLAS GEMV, the SwiGLU kernel and the residual add as
@@ -35,7 +37,7 @@ struct Unroll {
     static constexpr int value = MODE == 2 ? 4 : 8;
 };
 
-enum Mode { kStore = 0, kResidual = 1, kSwiglu = 2 };
+enum Mode { kStore = 0, kResidual = 1, kSwiglu = 2, kStoreF32 = 3 };
 
 __device__ __forceinline__ float dot8(uint4 w, uint4 a) {
     const __half2* wh = reinterpret_cast<const __half2*>(&w);
@@ -52,10 +54,11 @@ __device__ __forceinline__ float dot8(uint4 w, uint4 a) {
 }
 
 template <int MODE, bool NORM>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const __half* __restrict__ W, int64_t ldw, int N, int K,
-                                                        const __half* __restrict__ x,
+__global__ void __launch_bounds__(kThreads) gemv_kernel(const __half* __restrict__ W, const __half* __restrict__ W2,
+                                                        int64_t ldw, int N, int K, const __half* __restrict__ x,
                                                         const __half* __restrict__ rms_w, float eps,
-                                                        __half* __restrict__ out) {
+                                                        void* __restrict__ out_) {
+    __half* out = static_cast<__half*>(out_);
     extern __shared__ __align__(16) uint8_t gv_sm[];
     uint4* a_s = reinterpret_cast<uint4*>(gv_sm);  // K / 8 chunks of the input vector
     __shared__ float red[kWarps];
@@ -111,9 +114,11 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __half* __restrict
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
         // SWIGLU: rows 0..kRpw-1 are the gate rows n0+r, rows kRpw.. the up rows N+n0+r
+        // (or rows n0+r of W2)
         const int o = r % kRpw;
-        const int64_t row = (MODE == kSwiglu && r >= kRpw) ? (int64_t)N + n0 + o : (int64_t)n0 + o;
-        wr[r] = (n0 + o < N) ? W + row * ldw : nullptr;
+        const bool up = MODE == kSwiglu && r >= kRpw;
+        const int64_t row = (up && !W2) ? (int64_t)N + n0 + o : (int64_t)n0 + o;
+        wr[r] = (n0 + o < N) ? (up && W2 ? W2 : W) + row * ldw : nullptr;
     }
     float acc[NR];
 #pragma unroll
@@ -153,7 +158,9 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __half* __restrict
             }
         const int n = n0 + lane;
         const __half y16 = __float2half(yv);
-        if (MODE == kStore) {
+        if (MODE == kStoreF32) {
+            static_cast<float*>(out_)[n] = yv;
+        } else if (MODE == kStore) {
             out[n] = y16;
         } else if (MODE == kResidual) {
             out[n] = __float2half(__half2float(out[n]) + __half2float(y16));
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __half* __restrict
 }
 
 template <int MODE, bool NORM>
-static int launch(const fcci_gemv_desc* d, cudaStream_t st) {
+static int launch(const GemvArgs* d, cudaStream_t st) {
     const int rows_per_cta = kWarps * kRpw;
     const size_t smem = (size_t)d->K * 2;
     if (smem > 48 * 1024) {
@@ -186,25 +193,25 @@ static int launch(const fcci_gemv_desc* d, cudaStream_t st) {
     const int wave = device_sm_count(dev) * occ;
     if (wave > 0 && grid > wave) grid = wave;
     gemv_kernel<MODE, NORM><<<grid, kThreads, smem, st>>>(
-        static_cast<const __half*>(d->W), d->ld_w, d->N, d->K, static_cast<const __half*>(d->x),
-        static_cast<const __half*>(d->rms_w), d->eps, static_cast<__half*>(d->out));
+        static_cast<const __half*>(d->W), static_cast<const __half*>(d->W2), d->ld_w, d->N, d->K,
+        static_cast<const __half*>(d->x), static_cast<const __half*>(d->rms_w), d->eps, d->out);
     count_launch();
     return set_cuda_status(cudaGetLastError());
 }
 
 }  // namespace gv
-}  // namespace fcci
 
-extern "C" int fcci_gemv_fused(const fcci_gemv_desc* d, cudaStream_t stream) {
-    using namespace fcci;
+int gemv(const GemvArgs* d, cudaStream_t stream) {
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (!d || !d->W || !d->x || !d->out) return set_status(FCCI_EINVAL, "fcci_gemv_fused: NULL argument");
     if (d->N <= 0 || d->K <= 0 || (d->K & 7) || d->ld_w < d->K || (d->ld_w & 7))
         return set_status(FCCI_EINVAL, "fcci_gemv_fused: K and ld_w must be positive multiples of 8, ld_w >= K");
     if ((int64_t)d->K * 2 > 227 * 1024) return set_status(FCCI_EUNSUPPORTED, "fcci_gemv_fused: K too large");
-    if (!a16(d->W) || !a16(d->x) || (d->rms_w && !a16(d->rms_w)))
-        return set_status(FCCI_EINVAL, "fcci_gemv_fused: W, x and rms_w must be 16-byte aligned");
-    if ((reinterpret_cast<uintptr_t>(d->out) & 1)) return set_status(FCCI_EINVAL, "fcci_gemv_fused: out misaligned");
+    if (!a16(d->W) || !a16(d->x) || (d->rms_w && !a16(d->rms_w)) || (d->W2 && !a16(d->W2)))
+        return set_status(FCCI_EINVAL, "fcci_gemv_fused: W, W2, x and rms_w must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(d->out) & (d->mode == gv::kStoreF32 ? 3 : 1)))
+        return set_status(FCCI_EINVAL, "fcci_gemv_fused: out misaligned");
+    if (d->W2 && d->mode != gv::kSwiglu) return set_status(FCCI_EINVAL, "fcci_gemv_fused: W2 is for the SwiGLU mode");
     const bool norm = d->rms_w != nullptr;
     switch (d->mode * 2 + (norm ? 1 : 0)) {
         case 0: return gv::launch<gv::kStore, false>(d, stream);
@@ -213,6 +220,27 @@ extern "C" int fcci_gemv_fused(const fcci_gemv_desc* d, cudaStream_t stream) {
         case 3: return gv::launch<gv::kResidual, true>(d, stream);
         case 4: return gv::launch<gv::kSwiglu, false>(d, stream);
         case 5: return gv::launch<gv::kSwiglu, true>(d, stream);
-        default: return set_status(FCCI_EINVAL, "fcci_gemv_fused: mode must be 0, 1 or 2");
+        case 6: return gv::launch<gv::kStoreF32, false>(d, stream);
+        case 7: return gv::launch<gv::kStoreF32, true>(d, stream);
+        default: return set_status(FCCI_EINVAL, "fcci_gemv_fused: mode must be 0, 1, 2 or 3");
     }
+}
+
+}  // namespace fcci
+
+extern "C" int fcci_gemv_fused(const fcci_gemv_desc* d, cudaStream_t stream) {
+    if (!d) return fcci::set_status(FCCI_EINVAL, "fcci_gemv_fused: NULL argument");
+    if (d->mode < 0 || d->mode > 2) return fcci::set_status(FCCI_EINVAL, "fcci_gemv_fused: mode must be 0, 1 or 2");
+    fcci::GemvArgs a;
+    a.W = d->W;
+    a.W2 = nullptr;
+    a.ld_w = d->ld_w;
+    a.N = d->N;
+    a.K = d->K;
+    a.x = d->x;
+    a.rms_w = d->rms_w;
+    a.eps = d->eps;
+    a.out = d->out;
+    a.mode = d->mode;
+    return fcci::gemv(&a, stream);
 }

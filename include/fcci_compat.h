@@ -72,6 +72,63 @@ typedef struct fcci_gemv_desc {
 
 int fcci_gemv_fused(const fcci_gemv_desc* desc, cudaStream_t stream);
 
+/*
+ * The whole decode step of a Llama-2-shaped model for one token (batch 1). The
+ * reference's capture_decode_host_ext (custom_kernels/capture_decode_step_kernel.cu:
+ * 137-274) stands in for it with a layer-0 MLP on x = 0; this is the step in the order
+ * of the reference's decode driver (scripts/direct_custom_decode_500.py:208-296):
+ *
+ *   x = embed[token[0]]                        (a token outside [0, vocab) gives zeros)
+ *   per layer l:
+ *     qkv = W_qkv[l] . RMSNorm(x) * rms_in[l]  rows [q (Hq*D) | k (Hkv*D) | v (Hkv*D)]
+ *     RoPE(q, k) at T = seq_len[0]; arena_k/v[l, 0, :, T, :] = k_rot, v;
+ *     ctx = softmax(q k^T / sqrt(D)) v over keys 0..T      (GQA: head h reads h / (Hq/Hkv))
+ *     x  += W_o[l] . ctx
+ *     x  += W_down[l] . (SiLU(W_gate[l] . h) * (W_up[l] . h)),  h = RMSNorm(x) * rms_post[l]
+ *   logits = lm_head . RMSNorm(x) * rms_final  (fp32; lm_head NULL = tied to embed)
+ *   seq_len[0] = T + 1 (by the last layer's attention launch, after every read of T)
+ *
+ * Weights are row-major fp16 device matrices (the layout of the reference's
+ * weight_loader.load_and_pack: qkv_ptrs [(Hq+2Hkv)*D, hidden], o_ptrs [hidden, Hq*D],
+ * mlp_gate_ptrs / mlp_up_ptrs [I, hidden], mlp_down_ptrs [hidden, I]); the per-layer
+ * arrays are host arrays of device pointers, read during the call (a captured graph
+ * keeps the pointers of its capture). The arena is the reference's [layers, 1, Hkv,
+ * max_len, D] fp16. Scratch: x [hidden], qkv [(Hq+2Hkv)*D], ctx [Hq*D], act [I] fp16;
+ * workspace: fcci_decode_workspace_bytes(1, Hq, Hkv, D, device) bytes, zeroed once.
+ * Nothing is allocated and the host is not synchronised: the call can be captured.
+ */
+#define FCCI_LLAMA_STEP_ABI_VERSION 1
+typedef struct fcci_llama_step_desc {
+    int32_t abi_version; /* FCCI_LLAMA_STEP_ABI_VERSION */
+    int32_t layers, hidden, q_heads, kv_heads, head_dim, intermediate, vocab;
+    float rms_eps, rope_theta;
+    int32_t rotary_dim; /* -1: head_dim */
+    const int64_t* token;
+    const void* embed;
+    const void* const* w_qkv;
+    const void* const* w_o;
+    const void* const* w_gate;
+    const void* const* w_up;
+    const void* const* w_down;
+    const void* const* rms_in;
+    const void* const* rms_post;
+    const void* rms_final;
+    const void* lm_head;
+    void* arena_k;
+    void* arena_v;
+    int32_t max_len;
+    int32_t* seq_len;
+    void* x;
+    void* qkv;
+    void* ctx;
+    void* act;
+    float* logits;
+    void* workspace;
+    size_t workspace_bytes;
+} fcci_llama_step_desc;
+
+int fcci_llama_decode_step(const fcci_llama_step_desc* desc, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -98,7 +98,9 @@ extern "C" {
  *                      NULL only when advance == 0 and split == 0 (one CTA per
  *                      (sequence, kv head) pair, no partials).
  *   split              0: one CTA per (sequence, kv-head) pair; 1: persistent
- *                      stream-K split over all SMs with last-arriver combine.
+ *                      stream-K split over all SMs with last-arriver combine, or,
+ *                      with few pairs, one thread-block cluster per pair whose CTAs
+ *                      merge their pieces through distributed shared memory.
  *   flags              (abi_version >= 2) bit set of FCCI_DECODE_* below.
  *
  * Calls that share a workspace must not overlap on the GPU.
@@ -194,6 +196,10 @@ int fcci_decode_read_error(void* workspace, uint32_t* flags, int clear, cudaStre
 /* Tuning hook for measurements: pipeline stages per CTA (2..8) and persistent
  * CTAs per SM (1..2) of the split mode; 0 selects the automatic choice. */
 int fcci_decode_set_tuning(int stages, int ctas_per_sm);
+/* Measurement hook: largest thread-block cluster of the split mode's cluster launch
+ * (one cluster per (sequence, kv head) pair when there are at most half as many pairs
+ * as resident CTAs); 0 selects the automatic limit (16), 1 turns clusters off. */
+int fcci_decode_set_cluster_limit(int max_cluster);
 
 /* Status of the last call on this host thread, and its message. */
 int fcci_last_status(void);

@@ -251,25 +251,44 @@ def test_decode_long_split_kv(av):
     assert_close(got["out"], want["ctx"], "split-kv 32k")
 
 
+@pytest.mark.parametrize("max_cluster", [0, 8, 2, 1])
 @pytest.mark.parametrize("B,Hkv,G,T", [(32, 1, 8, 4095), (32, 2, 8, 4095), (1, 32, 1, 1000), (4, 8, 8, 4095)])
-def test_decode_pair_aligned_pieces(av, B, Hkv, G, T):
-    """Uniform lengths whose pairs the kernel cuts into pair-aligned pieces (the kv-head
-    shards of the 70B shape, and pairs x k CTAs with k dividing a pair's tiles): the piece
-    CTAs merge a slice each. Calls alternate with ragged lengths (stream-K pieces and the
-    single-merger path) on one workspace, so the pair counters must come back to zero."""
+def test_decode_few_pairs_cluster_and_stream_k(av, B, Hkv, G, T, max_cluster):
+    """Few (sequence, kv head) pairs: the split grid is launched as one thread-block cluster
+    per pair (up to max_cluster CTAs; 0 = automatic, 1 = no clusters). With uniform lengths
+    the CTAs of a cluster split the pair's tiles and merge their pieces through distributed
+    shared memory; calls alternate with ragged lengths (stream-K pieces, last-arriver merge)
+    on one workspace, so the pair counters must come back to zero."""
     D, cap = 128, T + 8
     ws = av.make_workspace(B, Hkv * G, Hkv, D)
-    for i, lens in enumerate([[T] * B, [max(1, T - 977 * b % T) for b in range(B)], [T] * B]):
-        q, kn, vn, kc, vc, lt, _ = make_case(B, Hkv, G, D, lens, cap, seed=700 + i)
-        dk, dv, dl = kc.to(DEV), vc.to(DEV), lt.to(DEV)
-        out = torch.full((B, Hkv * G, D), float("nan"), dtype=torch.float16, device=DEV)
-        av.decode(q.to(DEV), dk, dv, out, k_new=kn.to(DEV), v_new=vn.to(DEV), seq_lens=dl, advance=True,
-                  workspace=ws, split=True)
-        torch.cuda.synchronize()
-        assert av.read_error(ws) == 0
-        want = O.decode_step(q, kc, vc, lt, k_new=kn, v_new=vn)
-        assert_close(out.cpu(), want["ctx"], f"B={B} Hkv={Hkv} G={G} call {i}")
-        assert dl.cpu().tolist() == [t + 1 for t in lens]
+    av.set_tuning(max_cluster=max_cluster)
+    try:
+        for i, lens in enumerate([[T] * B, [max(1, T - 977 * b % T) for b in range(B)], [T] * B]):
+            q, kn, vn, kc, vc, lt, _ = make_case(B, Hkv, G, D, lens, cap, seed=700 + i)
+            dk, dv, dl = kc.to(DEV), vc.to(DEV), lt.to(DEV)
+            out = torch.full((B, Hkv * G, D), float("nan"), dtype=torch.float16, device=DEV)
+            av.decode(q.to(DEV), dk, dv, out, k_new=kn.to(DEV), v_new=vn.to(DEV), seq_lens=dl, advance=True,
+                      workspace=ws, split=True)
+            torch.cuda.synchronize()
+            assert av.read_error(ws) == 0
+            want = O.decode_step(q, kc, vc, lt, k_new=kn, v_new=vn)
+            assert_close(out.cpu(), want["ctx"], f"B={B} Hkv={Hkv} G={G} max_cluster={max_cluster} call {i}")
+            assert dl.cpu().tolist() == [t + 1 for t in lens]
+    finally:
+        av.set_tuning()
+
+
+@pytest.mark.parametrize("T", [0, 63, 64, 100, 700])
+def test_decode_cluster_short_pairs(av, T):
+    """Pairs of 1 to 12 tiles in a cluster launch: k_eff = min(k, tiles) CTAs carry the
+    pair (one tile each at most), the others only join the cluster barriers."""
+    B, Hkv, G, D = 2, 8, 8, 128
+    q, kn, vn, kc, vc, lt, _ = make_case(B, Hkv, G, D, [T] * B, T + 4, seed=750 + T)
+    got = run_decode(av, q, kn, vn, kc, vc, lt, None)
+    want = O.decode_step(q, kc, vc, lt, k_new=kn, v_new=vn)
+    assert got["err"] == 0
+    assert_close(got["out"], want["ctx"], f"T={T}")
+    assert got["lens"].tolist() == [T + 1] * B
 
 
 def test_decode_capacity_overflow_sets_error(av):

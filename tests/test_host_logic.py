@@ -108,52 +108,127 @@ def test_effective_ctas_on_the_measured_shapes():
     assert effective_ctas([4096] * 64, 32, 296) == 296   # more pairs than CTAs: stream-K
 
 
-COOP_PIECES = 6  # decode_attn.cu kCoopPieces
+MAX_CLUSTER = 16  # decode_attn.cu kMaxCluster
+
+
+def cluster_k(P, grid, fits=lambda k: True, max_cluster=MAX_CLUSTER, capacity=None):
+    """The host's choice of CTAs per cluster for a split launch (decode_attn.cu,
+    launch_decode_t): with at most half as many pairs as resident CTAs, the largest
+    k <= min(max_cluster, grid // P, tiles of the arena's capacity) for which P clusters
+    of k CTAs are resident at once (`fits`, the occupancy API on the device); 0 = no
+    clusters. capacity None stands for the packed layout (no per-sequence bound)."""
+    cap_tiles = MAX_CLUSTER if capacity is None else (capacity + TILE - 1) // TILE
+    if max_cluster < 2 or 2 * P > grid or cap_tiles < 2:
+        return 0
+    k = min(max_cluster, grid // P, cap_tiles)
+    while k >= 2 and not fits(k):
+        k -= 1
+    return k if k >= 2 else 0
+
+
+def cluster_ranges(lens, Hkv, k):
+    """Tile ranges of a cluster launch of P*k CTAs with uniform tile counts: CTA
+    x = pair*k + r takes part r of k_eff = min(k, tiles per pair) equal parts."""
+    pairs, N = decompose(lens, Hkv, 0)
+    P = len(pairs)
+    tp = N // P
+    k_eff = min(k, tp)
+    out = []
+    for x in range(P * k):
+        pr, r = divmod(x, k)
+        out.append((pr * tp + r * tp // k_eff, pr * tp + (r + 1) * tp // k_eff) if r < k_eff else (0, 0))
+    return out, k_eff
 
 
 def merge_mode(pairs, N, C, p):
-    """How pair p's pieces are merged (decode_attn.cu, segment end): 'whole' (one CTA),
-    'slices' (every piece ends its CTA's range and there are at least COOP_PIECES pieces:
-    the piece CTAs wait for one another and merge a slice each) or 'single' (the last
-    arriving piece merges all)."""
+    """How pair p's pieces are merged in a launch without clusters (decode_attn.cu,
+    segment end): 'whole' (one CTA) or 'single' (the last arriving piece merges all,
+    a counter nobody waits on)."""
     first, n = pairs[p]
     c0, c1 = cta_of_tile(first, N, C), cta_of_tile(first + n - 1, N, C)
-    if c0 == c1:
-        return "whole"
-    if c1 - c0 + 1 >= COOP_PIECES and first + n == (c1 + 1) * N // C:
-        return "slices"
-    return "single"
+    return "whole" if c0 == c1 else "single"
+
+
+def modes(lens, Hkv, grid=296):
+    """Merge modes of every pair of a split launch: 'cluster' when the host launches one
+    cluster per pair and the lengths give every pair the same tile count (pieces merged
+    through distributed shared memory), else those of merge_mode."""
+    P = len(lens) * Hkv
+    k = cluster_k(P, grid)
+    tiles = {tiles_of(L) for L in lens}
+    if k and len(tiles) == 1:
+        return {"whole" if min(k, tiles.pop()) == 1 else "cluster"}
+    g = P * k if k else grid
+    pairs, N = decompose(lens, Hkv, g)
+    C = min(g, N) if k else effective_ctas(lens, Hkv, g)
+    return {merge_mode(pairs, N, C, p) for p in range(len(pairs))}
 
 
 @pytest.mark.parametrize("seed", range(40))
-def test_slice_merge_never_holds_up_a_later_segment(seed):
-    rnd = random.Random(1000 + seed)
-    Hkv = rnd.choice([1, 2, 8, 32])
+def test_cluster_ranges_cover_each_pair_once(seed):
+    rnd = random.Random(2000 + seed)
+    Hkv = rnd.choice([1, 2, 4, 8, 32])
+    B = rnd.randint(1, 8)
     grid = rnd.choice([148, 296])
-    B = rnd.randint(1, 40)
-    lens = [rnd.choice([4096, 1000, 513, rnd.randint(1, 40000)])] * B if seed % 2 else \
-        [rnd.randint(1, 40000) for _ in range(B)]
-    pairs, N = decompose(lens, Hkv, grid)
-    C = effective_ctas(lens, Hkv, grid)
+    lens = [rnd.choice([0, 1, 63, 64, 65, 513, 4096, 32768, rnd.randint(1, 40000)])] * B
+    P = B * Hkv
+    k = cluster_k(P, grid)
+    if not k:
+        assert 2 * P > grid
+        return
+    assert 2 <= k <= MAX_CLUSTER and P * k <= grid
+    ranges, k_eff = cluster_ranges(lens, Hkv, k)
+    pairs, N = decompose(lens, Hkv, 0)
     for p, (first, n) in enumerate(pairs):
-        if merge_mode(pairs, N, C, p) != "slices":
-            continue
-        # every piece CTA's range ends inside this pair: waiting there delays nothing else
+        got = []
+        for r in range(k):
+            lo, hi = ranges[p * k + r]
+            if r < k_eff:
+                assert first <= lo < hi <= first + n  # never empty, never outside the pair
+                got.extend(range(lo, hi))
+            else:
+                assert lo == hi  # idle: joins the cluster barriers only
+        assert got == list(range(first, first + n))
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_cluster_launch_with_mixed_lengths_falls_back_to_stream_k(seed):
+    """Mixed tile counts in a cluster launch: stream-K over all P*k CTAs and last-arriver
+    merges; the piece slots stay inside the workspace sized for P + grid."""
+    rnd = random.Random(3000 + seed)
+    Hkv = rnd.choice([1, 2, 8])
+    B = rnd.randint(2, 8)
+    grid = 296
+    lens = [rnd.randint(1, 40000) for _ in range(B)]
+    k = cluster_k(B * Hkv, grid)
+    if not k:
+        return
+    g = B * Hkv * k
+    pairs, N = decompose(lens, Hkv, g)
+    C = min(g, N)
+    slots = set()
+    for p, (first, n) in enumerate(pairs):
         for c in range(cta_of_tile(first, N, C), cta_of_tile(first + n - 1, N, C) + 1):
-            assert first < (c + 1) * N // C <= first + n
+            assert p + c < len(pairs) + grid and p + c not in slots
+            slots.add(p + c)
 
 
 def test_merge_modes_on_the_measured_shapes():
-    def modes(lens, Hkv, grid=296):
-        pairs, N = decompose(lens, Hkv, grid)
-        C = effective_ctas(lens, Hkv, grid)
-        return {merge_mode(pairs, N, C, p) for p in range(len(pairs))}
     assert modes([4096] * 32, 8) == {"whole"}     # 70B shape on one GPU: one CTA per pair
-    assert modes([4096] * 32, 1) == {"slices"}    # 8-way kv-head shard: 9 pieces per pair
-    assert modes([4096] * 32, 2) == {"single"}    # 4-way shard: 4 pieces per pair
-    assert modes([4096] * 32, 4) == {"single"}    # 2-way shard: 2 pieces per pair
-    assert modes([32768] * 4, 8) == {"slices"}    # 4 x 32k keys
-    assert modes([1001], 32) == {"slices"}        # 1 x 32 heads x 1001 keys: 8 pieces per pair
+    assert cluster_k(32, 296) == 9                # 8-way kv-head shard: clusters of 9 CTAs
+    assert modes([4096] * 32, 1) == {"cluster"}
+    assert cluster_k(64, 296) == 4                # 4-way shard: clusters of 4
+    assert modes([4096] * 32, 2) == {"cluster"}
+    assert cluster_k(128, 296) == 2               # 2-way shard: pairs of CTAs
+    assert modes([4096] * 32, 4) == {"cluster"}
+    assert modes([32768] * 4, 8) == {"cluster"}   # 4 x 32k keys: clusters of 9
+    assert modes([512 + 1], 32) == {"cluster"}    # config 1 (one sequence, 32 heads): 9 tiles over 9 CTAs
+    assert modes([63], 32) == {"whole"}           # one tile per pair: no merge
+    assert "single" in modes([100, 20000], 8) <= {"single", "whole"}  # mixed: stream-K, last arriver
+    assert cluster_k(32, 296, fits=lambda k: k <= 8) == 8  # non-portable sizes unavailable
+    assert cluster_k(32, 296, capacity=140) == 3           # a short arena bounds the CTAs per pair
+    assert cluster_k(32, 296, capacity=64) == 0            # one tile at most: one CTA per pair
+    assert cluster_k(32, 296, max_cluster=1) == 0          # clusters turned off
 
 
 def test_partition_sequences_balances_bytes():
