@@ -208,6 +208,7 @@ def build_state(w, world, rank, seed=1234):
     else:
         kv_lo, kv_hi, q_lo, q_hi = partition_kv_heads(Hkv, Hq, world, rank)
         hkv, hq = kv_hi - kv_lo, q_hi - q_lo
+        q_lo_rank = q_lo
         lens = list(w["lens"])
         arena = fcci.KVArena(L, B, hkv, D, capacity=max(lens) + 1, q_heads=hq)
     b = len(lens)
@@ -224,14 +225,24 @@ def build_state(w, world, rank, seed=1234):
     vn = torch.randn(L, b, hkv, D, generator=g, device="cuda").half()
     out = torch.empty(L, b, hq, D, dtype=torch.float16, device="cuda")
     return dict(fcci=fcci, arena=arena, lens=lens, lens_dev=lens_dev, q=q, kn=kn, vn=vn, out=out, hq=hq, hkv=hkv,
-                b=b)
+                b=b, q_lo=q_lo_rank if not w["packed"] else 0)
 
 
 def run_step(st, gather=None):
     arena = st["arena"]
     arena.seq_lens.copy_(st["lens_dev"])
     L = arena.layers
+    ex = st.get("exchange")
     for l in range(L):
+        if ex is not None:
+            # the launch stores its ctx slice into every rank's full-ctx buffer, then the
+            # stream waits for every rank's slice of this layer
+            k, v = arena.layer(l)
+            ex.decode(st["q"][l], k, v, st["q_lo"], l, k_new=st["kn"][l], v_new=st["vn"][l],
+                      seq_lens=arena.seq_lens, advance=(l == L - 1), workspace=arena.workspace, split=True,
+                      prefetch_kv=st["prefetch_kv"])
+            ex.wait()
+            continue
         st["fcci"].decode_attention(arena, l, st["q"][l], st["out"][l], k_new=st["kn"][l], v_new=st["vn"][l],
                                     advance=(l == L - 1), prefetch_kv=st["prefetch_kv"])
         if gather is not None:
@@ -253,7 +264,7 @@ def capture_step_graph(st, gather=None):
     return graph
 
 
-def check_step(st, layer=0):
+def check_step(st, layer=0, out=None):
     """The timed step's answer at the timed shape: one layer's ctx of the last replay, on the
     first, middle and last sequence of this rank, against the fp32 oracle (max-abs 2e-3,
     relative-L2 1e-3). The appended row T is in the arena already; the oracle re-appends it."""
@@ -275,7 +286,8 @@ def check_step(st, layer=0):
         want = O.decode_step(st["q"][layer][i:i + 1].cpu(), kc, vc, torch.tensor([T], dtype=torch.int32),
                              k_new=st["kn"][layer][i:i + 1].cpu(), v_new=st["vn"][layer][i:i + 1].cpu(),
                              capacity=T + 1, inplace=True)
-        ma, rel = O.compare(st["out"][layer][i:i + 1].float().cpu(), want["ctx"])
+        got = (st["out"][layer] if out is None else out)[i:i + 1]
+        ma, rel = O.compare(got.float().cpu(), want["ctx"])
         worst_abs, worst_rel = max(worst_abs, ma), max(worst_rel, rel)
     ok = worst_abs <= O.MAX_ABS_TOL and worst_rel <= O.REL_L2_TOL
     return {"ok": ok, "layer": layer, "sequences": picks, "max_abs": worst_abs, "rel_l2": worst_rel,
@@ -405,13 +417,19 @@ def ours(args):
     st["prefetch_kv"] = not args.no_prefetch_kv
     L, D = w["layers"], w["D"]
     gather = None
-    if args.gather_ctx and world > 1:
-        from fully_custom_cuda_inference_lamma2_b200.sharding import gather_ctx
+    if args.gather_ctx and world > 1 and not w["packed"]:
+        if args.gather_impl == "nccl":
+            from fully_custom_cuda_inference_lamma2_b200.sharding import gather_ctx
 
-        full = torch.empty(L, st["b"], w["Hq"], D, dtype=torch.float16, device="cuda")
+            full = torch.empty(L, st["b"], w["Hq"], D, dtype=torch.float16, device="cuda")
+            stage = torch.empty(world, st["b"], st["hq"], D, dtype=torch.float16, device="cuda")
 
-        def gather(l):
-            gather_ctx(st["out"][l], out=full[l])
+            def gather(l):
+                gather_ctx(st["out"][l], out=full[l], stage=stage)
+        else:
+            from fully_custom_cuda_inference_lamma2_b200.sharding import CtxExchange
+
+            st["exchange"] = CtxExchange(st["b"], w["Hq"], D)
 
     graph = capture_step_graph(st, gather)
     for _ in range(args.warmup):
@@ -450,8 +468,13 @@ def ours(args):
     hbm, hbm_src = peaks()
     clocks = clk.summary()
 
-    # ---- the answer of the timed step, checked against the oracle on every rank
-    checked = check_step(st)
+    # ---- the answer of the timed step, checked against the oracle on every rank (with the
+    #      exchange, this rank's slice of the last layer's full-ctx buffer)
+    ex = st.get("exchange")
+    if ex is None:
+        checked = check_step(st)
+    else:
+        checked = check_step(st, L - 1, ex.buffer(L - 1)[:, st["q_lo"]:st["q_lo"] + st["hq"]])
     ok_all = checked["ok"]
     if world > 1:
         import torch.distributed as dist
@@ -484,6 +507,11 @@ def ours(args):
 
     del graph
     barrier(world)
+    if st.get("exchange") is not None:
+        if st["exchange"].error():
+            print("bench: the ctx exchange timed out on the device", file=sys.stderr, flush=True)
+            ok_all = False
+        st["exchange"].close()
     if not ok_all:
         if rank == 0:
             print(f"bench: the timed step's ctx differs from the oracle: {checked}", file=sys.stderr, flush=True)
@@ -533,7 +561,7 @@ def ours(args):
             "kv_len": (w["lens"][0] if len(set(w["lens"])) == 1 else "seeded U[128,8192]"), "layers": L,
             "parallelism": ("kv-head shards x%d" % world) if not w["packed"] else ("sequence shards x%d" % world),
             "shard_of": args.shard_of if world == 1 and args.shard_of > 1 else None,
-            "gather_ctx": bool(args.gather_ctx and world > 1),
+            "gather_ctx": (args.gather_impl if args.gather_ctx and world > 1 and not w["packed"] else False),
             "prefetch_kv": not args.no_prefetch_kv,
             "max_cluster": args.max_cluster or "auto",
             "l2": "no flush: arena %.1f GB per GPU > 126 MB L2" % arena_gb,
@@ -1233,7 +1261,10 @@ def main():
     ap.add_argument("--workload", default="gqa70b",
                     choices=["gqa70b", "gqa70b_32k", "varlen7b", "mha7b", "prefill16", "llama7b"])
     ap.add_argument("--layers", type=int, default=None)
-    ap.add_argument("--gather-ctx", action="store_true")
+    ap.add_argument("--gather-ctx", action="store_true",
+                    help="kv-head shards: every rank also gets the full ctx of every layer (an unsharded O-proj)")
+    ap.add_argument("--gather-impl", choices=["peer", "nccl"], default="peer",
+                    help="peer: stores fused into the decode launch over NVLink; nccl: all-gather after it")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="with one GPU: run rank 0's share of an N-way partition of the workload (profiling)")
     ap.add_argument("--no-prefetch-kv", action="store_true",
@@ -1242,6 +1273,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--max-cluster", type=int, default=0,
                     help="largest thread-block cluster of the split decode launch (0 automatic, 1 none)")
+    ap.add_argument("--solo-tiles", type=int, default=-1,
+                    help="pairs of at most this many tiles are not split in a cluster launch (-1 automatic)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (A/B measurements)")
     ap.add_argument("--kv-len", type=int, default=0, help="decode workloads: every sequence at this many keys")
     ap.add_argument("--no-subrecords", action="store_true",
@@ -1249,10 +1282,10 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.max_cluster and args.impl == "ours":
+    if (args.max_cluster or args.solo_tiles >= 0) and args.impl == "ours":
         import fully_custom_cuda_inference_lamma2_b200 as fcci
 
-        fcci.attn_varlen.set_tuning(max_cluster=args.max_cluster)
+        fcci.attn_varlen.set_tuning(max_cluster=args.max_cluster, solo_tiles=args.solo_tiles)
     if args.workload == "llama7b":
         (llama_reference if args.impl == "reference" else llama_ours)(args)
     elif args.workload == "prefill16":

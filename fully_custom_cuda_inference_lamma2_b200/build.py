@@ -27,7 +27,7 @@ NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 LIB = os.path.join(PKG, "libfcci_decode.so")
-LIB_SOURCES = ["decode_attn.cu", "capi.cu", "compat.cu", "noalloc.cu", "prefill_attn.cu", "gemv.cu", "step.cu"]
+LIB_SOURCES = ["decode_attn.cu", "capi.cu", "compat.cu", "noalloc.cu", "prefill_attn.cu", "gemv.cu", "step.cu", "exchange.cu"]
 LIB_HEADERS = ["ptx.cuh", "tcgen05.cuh", "fcci_internal.h"]
 MODULES = {
     "attn_varlen": "attn_varlen_module.cpp",
@@ -56,7 +56,7 @@ def _run(cmd: list[str], cwd: str | None = None) -> None:
 
 
 def _common_headers() -> list[str]:
-    return [os.path.join(INCLUDE, h) for h in ("fcci_decode.h", "fcci_compat.h", "fcci_prefill.h")]
+    return [os.path.join(INCLUDE, h) for h in ("fcci_decode.h", "fcci_compat.h", "fcci_prefill.h", "fcci_exchange.h")]
 
 
 def build_library(force: bool = False) -> str:

@@ -2,7 +2,13 @@
 // custom_kernels/attn_varlen.cpp:16-49) plus allocation-free and batched entry
 // points, all launching the sm_100a kernels of libfcci_decode.so on the current
 // CUDA stream.
+#include <pybind11/stl.h>
+
+#include <string>
+#include <vector>
+
 #include "binding_common.h"
+#include "fcci_exchange.h"
 #include "fcci_prefill.h"
 
 using namespace fcci_py;
@@ -88,7 +94,9 @@ void forward_out(at::Tensor q, at::Tensor k, at::Tensor v, int64_t seq_len, doub
 void decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor out, c10::optional<at::Tensor> k_new,
             c10::optional<at::Tensor> v_new, c10::optional<at::Tensor> seq_lens, c10::optional<at::Tensor> cu_seqlens,
             int64_t fixed_len, double scale, double rope_theta, int64_t rotary_dim, bool advance,
-            c10::optional<at::Tensor> workspace, c10::optional<at::Tensor> q_rot_out, bool split, bool prefetch_kv) {
+            c10::optional<at::Tensor> workspace, c10::optional<at::Tensor> q_rot_out, bool split, bool prefetch_kv,
+            const std::vector<uint64_t>& peer_out, const std::vector<uint64_t>& peer_flags, uint64_t exch_flags,
+            uint64_t exch_epoch, int64_t exch_rank) {
     check_half_cuda(q, "q");
     check_half_cuda(k_cache, "k_cache");
     check_half_cuda(v_cache, "v_cache");
@@ -184,10 +192,30 @@ void decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor out
     d.advance = advance ? 1 : 0;
     at::Tensor ws;
     if (workspace.has_value() && workspace->defined()) ws = *workspace;
-    else if (split || advance) ws = cached_workspace(B, Hq, Hkv, D, q.device());
+    else if (split || advance || exch_rank >= 0) ws = cached_workspace(B, Hq, Hkv, D, q.device());
     if (ws.defined()) bind_workspace(d, ws);
     d.split = split ? 1 : 0;
     d.flags = prefetch_kv ? FCCI_DECODE_PREFETCH_KV : 0u;
+    if (exch_rank >= 0) {
+        // ctx exchange: `out` is this rank's slice of its full-ctx buffer; the peers'
+        // mappings receive the same slice at the same offsets
+        TORCH_CHECK(!peer_out.empty() && peer_out.size() == peer_flags.size() && peer_out.size() <= FCCI_MAX_PEERS,
+                    "peer_out and peer_flags: one entry per peer (1..7)");
+        TORCH_CHECK(exch_flags != 0 && exch_epoch != 0, "exch_flags and exch_epoch are required");
+        TORCH_CHECK(ws.defined(), "the exchange needs a workspace");
+        fcci_ctx_exchange ex;
+        std::memset(&ex, 0, sizeof(ex));
+        ex.n_peers = (int32_t)peer_out.size();
+        ex.rank = (int32_t)exch_rank;
+        for (size_t i = 0; i < peer_out.size(); ++i) {
+            ex.peer_out[i] = reinterpret_cast<void*>(peer_out[i]);
+            ex.peer_flags[i] = reinterpret_cast<uint32_t*>(peer_flags[i]);
+        }
+        ex.flags = reinterpret_cast<uint32_t*>(exch_flags);
+        ex.epoch = reinterpret_cast<uint32_t*>(exch_epoch);
+        check_rc(fcci_decode_attention_exchange(&d, &ex, current_stream()), "attn_varlen.decode (exchange)");
+        return;
+    }
     check_rc(fcci_decode_attention(&d, current_stream()), "attn_varlen.decode");
 }
 
@@ -390,7 +418,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("v_new") = py::none(), py::arg("seq_lens") = py::none(), py::arg("cu_seqlens") = py::none(),
           py::arg("fixed_len") = -1, py::arg("scale") = -1.0, py::arg("rope_theta") = 10000.0,
           py::arg("rotary_dim") = -1, py::arg("advance") = false, py::arg("workspace") = py::none(),
-          py::arg("q_rot_out") = py::none(), py::arg("split") = true, py::arg("prefetch_kv") = false);
+          py::arg("q_rot_out") = py::none(), py::arg("split") = true, py::arg("prefetch_kv") = false, py::kw_only(),
+          py::arg("peer_out") = std::vector<uint64_t>(), py::arg("peer_flags") = std::vector<uint64_t>(),
+          py::arg("exch_flags") = 0, py::arg("exch_epoch") = 0, py::arg("exch_rank") = -1);
     m.def("rope_append", &rope_append, "RoPE(q,k_new) at T and append of k/v at T (no attention)", py::arg("q"),
           py::arg("k_new"), py::arg("v_new"), py::arg("k_cache"), py::arg("v_cache"), py::arg("seq_lens"),
           py::arg("cu_seqlens") = py::none(), py::arg("rope_theta") = 10000.0, py::arg("rotary_dim") = -1,
@@ -443,16 +473,56 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         },
         py::arg("workspace"), py::arg("clear") = true);
     m.def("launch_count", []() { return (int64_t)fcci_launch_count(); });
+    // ctx exchange plumbing (fcci_exchange.h): IPC buffers and the bounded flag wait
+    m.def(
+        "ipc_alloc",
+        [](int64_t nbytes, c10::optional<at::Device> device) {
+            at::Device dev = device.has_value() ? *device : at::Device(at::kCUDA, c10::cuda::current_device());
+            c10::cuda::CUDAGuard guard(dev);
+            void* ptr = nullptr;
+            std::string handle(FCCI_IPC_HANDLE_BYTES, '\0');
+            check_rc(fcci_ipc_alloc((size_t)nbytes, &ptr, &handle[0]), "ipc_alloc");
+            at::Tensor t = at::from_blob(
+                ptr, {nbytes}, [](void* p) { fcci_ipc_free(p); }, at::TensorOptions().dtype(at::kByte).device(dev));
+            return py::make_tuple(t, py::bytes(handle));
+        },
+        "Zeroed device buffer that peer processes can map, and its IPC handle (bytes)", py::arg("nbytes"),
+        py::arg("device") = py::none());
+    m.def(
+        "ipc_open",
+        [](py::bytes handle) {
+            std::string h = handle;
+            TORCH_CHECK(h.size() == FCCI_IPC_HANDLE_BYTES, "ipc_open: handle must be ", FCCI_IPC_HANDLE_BYTES, " bytes");
+            void* ptr = nullptr;
+            check_rc(fcci_ipc_open(h.data(), &ptr), "ipc_open");
+            return (uint64_t)reinterpret_cast<uintptr_t>(ptr);
+        },
+        "Map a peer process's buffer on the current device; returns its device address");
+    m.def(
+        "ipc_close", [](uint64_t ptr) { check_rc(fcci_ipc_close(reinterpret_cast<void*>(ptr)), "ipc_close"); },
+        "Unmap a buffer opened with ipc_open");
+    m.def(
+        "exchange_wait",
+        [](at::Tensor flags, int64_t n, at::Tensor epoch, at::Tensor err, int64_t limit_ns) {
+            TORCH_CHECK(flags.is_cuda() && epoch.is_cuda() && err.is_cuda(), "exchange_wait: CUDA tensors");
+            c10::cuda::CUDAGuard guard(flags.device());
+            check_rc(fcci_exchange_wait(static_cast<const uint32_t*>(flags.data_ptr()), (int)n,
+                                        static_cast<const uint32_t*>(epoch.data_ptr()),
+                                        static_cast<uint32_t*>(err.data_ptr()), (uint64_t)limit_ns, current_stream()),
+                     "exchange_wait");
+        },
+        "Hold the current stream until every flag has reached the epoch (bounded; timeout bit in err)",
+        py::arg("flags"), py::arg("n"), py::arg("epoch"), py::arg("err"), py::arg("limit_ns") = 1000000000);
     m.def("clear_workspace_cache", &clear_workspace_cache,
           "Drop the workspaces kept for calls made without one (forward, capture_decode with q); "
           "needed only after a device timeout");
     m.def(
         "set_tuning",
-        [](int64_t stages, int64_t ctas, int64_t max_cluster) {
+        [](int64_t stages, int64_t ctas, int64_t max_cluster, int64_t solo_tiles) {
             check_rc(fcci_decode_set_tuning((int)stages, (int)ctas), "set_tuning");
-            check_rc(fcci_decode_set_cluster_limit((int)max_cluster), "set_tuning");
+            check_rc(fcci_decode_set_cluster_limit((int)max_cluster, (int)solo_tiles), "set_tuning");
         },
-        "Measurement hook: pipeline stages, CTAs per SM and the largest cluster of the split mode (0 = automatic, "
-        "max_cluster 1 = no clusters)",
-        py::arg("stages") = 0, py::arg("ctas_per_sm") = 0, py::arg("max_cluster") = 0);
+        "Measurement hook: pipeline stages, CTAs per SM, the largest cluster of the split mode (0 = automatic, "
+        "max_cluster 1 = no clusters) and the tiles up to which a pair is not split in a cluster (-1 = automatic)",
+        py::arg("stages") = 0, py::arg("ctas_per_sm") = 0, py::arg("max_cluster") = 0, py::arg("solo_tiles") = -1);
 }

@@ -49,6 +49,7 @@
 #include <tuple>
 
 #include "fcci_decode.h"
+#include "fcci_exchange.h"
 #include "fcci_internal.h"
 #include "ptx.cuh"
 
@@ -63,6 +64,7 @@ constexpr int kBoxBytes = kGroupKeys * 128;  // 16 rows x 64 fp16
 constexpr int kHalfTileBytes = kTileKeys * 128;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any healthy wait
 constexpr int kMaxCluster = 16;  // CTAs per cluster of a cluster launch (non-portable above 8)
+constexpr int kSoloTiles = 2;     // pairs of at most this many tiles are not split in a cluster launch
 constexpr uint64_t kDrainLimitNs = 500000000ull;
 constexpr int kConsumerBar = 1;
 
@@ -92,6 +94,14 @@ struct Params {
     int32_t split;
     int32_t prefetch_kv;  // FCCI_DECODE_PREFETCH_KV: lengths and the first stages before griddepcontrol.wait
     int32_t cluster_k;    // CTAs per cluster of a split launch in clusters of one pair each; 0 otherwise
+    int32_t solo_tiles;   // in such a launch, pairs of at most this many tiles stay on one CTA
+    // ctx exchange (fcci_exchange.h): the slice also goes to n_peers peers' buffers at the
+    // offsets it has in `out`; the last CTA raises slot xrank of every flag array
+    int32_t n_peers, xrank;
+    __half* peer_out[FCCI_MAX_PEERS];
+    uint32_t* peer_flags[FCCI_MAX_PEERS];
+    uint32_t* xflags;
+    uint32_t* xepoch;
     int32_t B, Hq, Hkv, G;
     int32_t stages;
     uint32_t* err;
@@ -128,6 +138,26 @@ __device__ __forceinline__ SeqInfo seq_info(const Params& p, int b) {
 }
 
 __device__ __forceinline__ int tiles_of(int L) { return L > 0 ? (L + kTileKeys - 1) / kTileKeys : 1; }
+
+// ctx element(s) at element offset `off` of `out`, and of every peer's buffer when the
+// launch exchanges ctx (static peer indices: the parameter array stays in param space)
+__device__ __forceinline__ void store_ctx2(const Params& p, int64_t off, __half2 v) {
+    *reinterpret_cast<__half2*>(p.out + off) = v;
+#pragma unroll
+    for (int i = 0; i < FCCI_MAX_PEERS; ++i)
+        if (i < p.n_peers) *reinterpret_cast<__half2*>(p.peer_out[i] + off) = v;
+}
+
+__device__ __forceinline__ void store_ctx1(const Params& p, int64_t off, __half v) {
+    p.out[off] = v;
+#pragma unroll
+    for (int i = 0; i < FCCI_MAX_PEERS; ++i)
+        if (i < p.n_peers) p.peer_out[i][off] = v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
 
 __device__ __forceinline__ void set_error(const Params& p, uint32_t bit) {
     if (p.err) atomicOr(p.err, bit);
@@ -319,6 +349,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
             cmode = true;
             const long long tp = N / P;
             k_eff = (int)(tp < ck ? tp : ck);
+            if (tp <= p.solo_tiles) k_eff = 1;
             const long long pr = blockIdx.x / ck;
             const int r = (int)(blockIdx.x % ck);
             C = P * k_eff;
@@ -705,7 +736,6 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     whole = (c0 == c1);
                 }
                 const int slot = pidx + blockIdx.x;
-                __half* ob = p.out + (int64_t)b * p.o_sb;
                 for (int e = ctid * 2; e < G * D; e += 2 * kConsumerThreads) {
                     const int hh = e / D;
                     const int d = e - hh * D;
@@ -724,8 +754,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     }
                     const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
                     if (whole) {
-                        *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) =
-                            __floats2half2_rn(o0 * inv, o1 * inv);
+                        store_ctx2(p, (int64_t)b * p.o_sb + (int64_t)(h * G + hh) * p.o_sh + d,
+                                   __floats2half2_rn(o0 * inv, o1 * inv));
                     } else if (cmode) {
                         *reinterpret_cast<float2*>(xo + hh * D + d) = make_float2(o0 * inv, o1 * inv);
                         if (d == 0) xl[hh] = Ls > 0.f ? M + __log2f(Ls) : -INFINITY;
@@ -799,8 +829,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                                 const int hh = e / D;
                                 const int d = e - hh * D;
                                 const float inv = Wt[k] > 0.f ? 1.f / Wt[k] : 0.f;
-                                *reinterpret_cast<__half2*>(ob + (int64_t)(h * G + hh) * p.o_sh + d) =
-                                    __floats2half2_rn(Ov[k].x * inv, Ov[k].y * inv);
+                                store_ctx2(p, (int64_t)b * p.o_sb + (int64_t)(h * G + hh) * p.o_sh + d,
+                                           __floats2half2_rn(Ov[k].x * inv, Ov[k].y * inv));
                             }
                         }
                         if (ctid == 0) atomicExch(&p.pair_cnt[pidx], 0u);
@@ -836,7 +866,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         if (cmode && k_eff > 1 && r < k_eff && warp < kConsumerWarps) {
             const int pr = (int)(blockIdx.x / ck);
             const int mb = pr / Hkv, mh = pr - mb * Hkv;
-            __half* obm = p.out + (int64_t)mb * p.o_sb + (int64_t)(mh * G) * p.o_sh;
+            const int64_t obm = (int64_t)mb * p.o_sb + (int64_t)(mh * G) * p.o_sh;
             const int E = G * D;
             const int lo = (int)((long long)r * E / k_eff), hi = (int)((long long)(r + 1) * E / k_eff);
             const uint32_t xo_s = smem_u32(xo), xl_s = smem_u32(xl);
@@ -863,13 +893,20 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                     }
                 }
                 const float inv = Wt > 0.f ? 1.f / Wt : 0.f;
-                obm[(int64_t)hh * p.o_sh + d] = __float2half_rn(Ov * inv);
+                store_ctx1(p, obm + (int64_t)hh * p.o_sh + d, __float2half_rn(Ov * inv));
             }
         }
         cluster_sync_all();
     }
-    // ---- device-side seq_len advance once every CTA has read the lengths
-    if (p.advance) {
+    // ---- ctx exchange: every thread's stores to the peers become visible system-wide
+    //      before its CTA counts in below
+    if (p.n_peers > 0) {
+        __threadfence_system();
+        __syncthreads();
+    }
+    // ---- the last CTA: device-side seq_len advance (once every CTA has read the
+    //      lengths) and the exchange's flag raise (once every CTA has stored its ctx)
+    if (p.advance || p.n_peers > 0) {
         if (tid == 0) {
             __threadfence();
             const unsigned old = atomicAdd(p.done_cnt, 1u);
@@ -878,11 +915,24 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         __syncthreads();
         if (misc[1]) {
             __threadfence();
-            for (int b = tid; b < B; b += kThreads) {
-                const SeqInfo si = seq_info(p, b);
-                if (si.ok) p.seq_lens[b] = si.T + 1;
+            if (p.advance) {
+                for (int b = tid; b < B; b += kThreads) {
+                    const SeqInfo si = seq_info(p, b);
+                    if (si.ok) p.seq_lens[b] = si.T + 1;
+                }
             }
-            if (tid == 0) atomicExch(p.done_cnt, 0u);
+            if (tid == 0) {
+                if (p.n_peers > 0) {
+                    const uint32_t e = *p.xepoch + 1u;
+                    *p.xepoch = e;
+                    __threadfence_system();
+#pragma unroll
+                    for (int i = 0; i < FCCI_MAX_PEERS; ++i)
+                        if (i < p.n_peers) st_release_sys(p.peer_flags[i] + p.xrank, e);
+                    st_release_sys(p.xflags + p.xrank, e);
+                }
+                atomicExch(p.done_cnt, 0u);
+            }
         }
     }
 }
@@ -1135,6 +1185,7 @@ static int launch_decode_t(Params prm, const CUtensorMap& mk, const CUtensorMap&
             while (k >= 2 && !clusters_fit<D, NB>((int)k, P, smem, dev, non_portable[dev])) --k;
             if (k >= 2) {
                 prm.cluster_k = (int)k;
+                prm.solo_tiles = g_tuning.solo_tiles >= 0 ? g_tuning.solo_tiles : kSoloTiles;
                 grid = (int)(P * k);
             }
         }
@@ -1264,10 +1315,20 @@ static void bind_workspace(Params& p, void* ws, const WorkspaceLayout& L) {
     p.part_o = reinterpret_cast<float*>(base + L.part_o);
 }
 
-int decode_attention(const fcci_decode_desc* d, cudaStream_t stream) {
+int decode_attention(const fcci_decode_desc* d, cudaStream_t stream, const fcci_ctx_exchange* ex) {
     Params p;
     int rc = fill_params(d, p, true);
     if (rc) return rc;
+    if (ex) {
+        p.n_peers = ex->n_peers;
+        p.xrank = ex->rank;
+        for (int i = 0; i < ex->n_peers; ++i) {
+            p.peer_out[i] = static_cast<__half*>(ex->peer_out[i]);
+            p.peer_flags[i] = ex->peer_flags[i];
+        }
+        p.xflags = ex->flags;
+        p.xepoch = ex->epoch;
+    }
     const int G = p.G;
     const int NB = G <= 8 ? 1 : (G <= 16 ? 2 : 0);
     if (NB == 0 || (d->D == 256 && NB == 2))
@@ -1289,7 +1350,7 @@ int decode_attention(const fcci_decode_desc* d, cudaStream_t stream) {
         if (pairs > 0x7fffffff) return set_status(FCCI_EINVAL, "fcci_decode_attention: too many pairs");
         grid = (int)pairs;
     }
-    const bool need_ws = split || p.advance;
+    const bool need_ws = split || p.advance || p.n_peers > 0;
     if (need_ws) {
         const WorkspaceLayout L = workspace_layout(p.B, p.Hq, p.Hkv, d->D, sms * kMaxCtasPerSm);
         if (!d->workspace || d->workspace_bytes < L.total)

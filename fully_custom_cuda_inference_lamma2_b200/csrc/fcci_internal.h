@@ -8,6 +8,7 @@
 #include <utility>
 
 #include "fcci_decode.h"
+#include "fcci_exchange.h"
 
 namespace fcci {
 
@@ -18,6 +19,7 @@ struct Tuning {
     int stages = 0;       // pipeline depth (64-key K+V tiles per CTA); 0 = automatic
     int ctas_per_sm = 0;  // persistent CTAs per SM in split mode; 0 = automatic
     int max_cluster = 0;  // largest cluster of a split launch; 0 = automatic (16), 1 = no clusters
+    int solo_tiles = -1;  // pairs of at most this many tiles stay on one CTA of their cluster; -1 = automatic
 };
 Tuning& tuning();
 
@@ -35,7 +37,8 @@ int encode_f16_sw128(CUtensorMap* map, const void* base, int rank, const uint64_
 int set_cuda_status(cudaError_t e);
 void count_launch();
 
-int decode_attention(const fcci_decode_desc* d, cudaStream_t stream);
+// ex (nullable): the ctx exchange of fcci_decode_attention_exchange
+int decode_attention(const fcci_decode_desc* d, cudaStream_t stream, const fcci_ctx_exchange* ex = nullptr);
 
 // Launch `kernel` with programmatic stream serialization: it may start while the
 // previous kernel of the stream finishes, and must call griddepcontrol.wait before

@@ -198,8 +198,10 @@ int fcci_decode_read_error(void* workspace, uint32_t* flags, int clear, cudaStre
 int fcci_decode_set_tuning(int stages, int ctas_per_sm);
 /* Measurement hook: largest thread-block cluster of the split mode's cluster launch
  * (one cluster per (sequence, kv head) pair when there are at most half as many pairs
- * as resident CTAs); 0 selects the automatic limit (16), 1 turns clusters off. */
-int fcci_decode_set_cluster_limit(int max_cluster);
+ * as resident CTAs); 0 selects the automatic limit (16), 1 turns clusters off. In such
+ * a launch pairs of at most solo_tiles 64-key tiles are carried by one CTA of their
+ * cluster instead of being split; -1 selects the automatic threshold. */
+int fcci_decode_set_cluster_limit(int max_cluster, int solo_tiles);
 
 /* Status of the last call on this host thread, and its message. */
 int fcci_last_status(void);

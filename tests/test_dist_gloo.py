@@ -43,6 +43,11 @@ def _worker(rank, world, port, q):
                              k_new=kn[:, kv_lo:kv_hi], v_new=vn[:, kv_lo:kv_hi])["ctx"]
         gathered = sharding.gather_ctx(part)
         ok_heads = torch.allclose(gathered, full, atol=1e-6)
+        # the same into caller-owned buffers (nothing allocated per call)
+        stage = torch.empty(world, B, q_hi - q_lo, D)
+        out = torch.empty(B, Hq, D)
+        sharding.gather_ctx(part, out=out, stage=stage)
+        ok_heads = ok_heads and torch.allclose(out, full, atol=1e-6)
         # sequence shards: each rank computes its own sequences, results identical
         mine = sharding.partition_sequences(lens.tolist(), world)[rank]
         sub = O.decode_step(qq[mine], kc[mine], vc[mine], lens[mine], k_new=kn[mine], v_new=vn[mine])["ctx"]

@@ -109,6 +109,7 @@ def test_effective_ctas_on_the_measured_shapes():
 
 
 MAX_CLUSTER = 16  # decode_attn.cu kMaxCluster
+SOLO_TILES = 2    # decode_attn.cu kSoloTiles
 
 
 def cluster_k(P, grid, fits=lambda k: True, max_cluster=MAX_CLUSTER, capacity=None):
@@ -126,13 +127,14 @@ def cluster_k(P, grid, fits=lambda k: True, max_cluster=MAX_CLUSTER, capacity=No
     return k if k >= 2 else 0
 
 
-def cluster_ranges(lens, Hkv, k):
+def cluster_ranges(lens, Hkv, k, solo=SOLO_TILES):
     """Tile ranges of a cluster launch of P*k CTAs with uniform tile counts: CTA
-    x = pair*k + r takes part r of k_eff = min(k, tiles per pair) equal parts."""
+    x = pair*k + r takes part r of k_eff = min(k, tiles per pair) equal parts, or the
+    whole pair (k_eff = 1) when it has at most `solo` tiles."""
     pairs, N = decompose(lens, Hkv, 0)
     P = len(pairs)
     tp = N // P
-    k_eff = min(k, tp)
+    k_eff = 1 if tp <= solo else min(k, tp)
     out = []
     for x in range(P * k):
         pr, r = divmod(x, k)
@@ -157,7 +159,8 @@ def modes(lens, Hkv, grid=296):
     k = cluster_k(P, grid)
     tiles = {tiles_of(L) for L in lens}
     if k and len(tiles) == 1:
-        return {"whole" if min(k, tiles.pop()) == 1 else "cluster"}
+        tp = tiles.pop()
+        return {"whole" if tp <= SOLO_TILES or min(k, tp) == 1 else "cluster"}
     g = P * k if k else grid
     pairs, N = decompose(lens, Hkv, g)
     C = min(g, N) if k else effective_ctas(lens, Hkv, g)
@@ -224,6 +227,7 @@ def test_merge_modes_on_the_measured_shapes():
     assert modes([32768] * 4, 8) == {"cluster"}   # 4 x 32k keys: clusters of 9
     assert modes([512 + 1], 32) == {"cluster"}    # config 1 (one sequence, 32 heads): 9 tiles over 9 CTAs
     assert modes([63], 32) == {"whole"}           # one tile per pair: no merge
+    assert modes([100], 32) == {"whole"}          # two tiles: one CTA of each cluster carries the pair
     assert "single" in modes([100, 20000], 8) <= {"single", "whole"}  # mixed: stream-K, last arriver
     assert cluster_k(32, 296, fits=lambda k: k <= 8) == 8  # non-portable sizes unavailable
     assert cluster_k(32, 296, capacity=140) == 3           # a short arena bounds the CTAs per pair
@@ -273,3 +277,29 @@ def test_bench_algorithmic_work_per_launch():
     p = bench.prefill_workload("prefill16", None)
     assert sum(p["lens"]) == 39_876
     assert bench.prefill_flops(p["Hq"], p["D"], p["lens"]) == 937_470_803_968
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_exchange_slices_tile_every_full_ctx_buffer(world):
+    """Each rank's slice of a full-ctx buffer (kv-head partition, slice_offset with the
+    decode kernel's out strides [Hq*D, D, 1]) covers its own heads of every sequence;
+    together the ranks cover each buffer exactly once, and the flag array, epoch and
+    error word sit after the buffers, 256-byte aligned (exchange_layout)."""
+    B, Hkv, G, D = 3, 8, 8, 128
+    Hq = Hkv * G
+    L = sharding.exchange_layout(B, Hq, D, world)
+    owner = {}
+    for buf in range(L["buffers"]):
+        for rank in range(world):
+            kv_lo, kv_hi, q_lo, q_hi = sharding.partition_kv_heads(Hkv, Hq, world, rank)
+            off = sharding.slice_offset(B, Hq, D, q_lo, buf)
+            assert off % 4 == 0
+            for b in range(B):
+                for h in range(q_hi - q_lo):
+                    e0 = off // 2 + b * Hq * D + h * D  # element index in the allocation
+                    for e in (e0, e0 + D - 1):
+                        assert e not in owner
+                        owner[e] = rank
+    assert len(owner) == 2 * L["buffers"] * B * Hq
+    assert L["flags"] >= L["buffers"] * L["ctx_bytes"] and L["flags"] % 256 == 0
+    assert L["epoch"] >= L["flags"] + 4 * world and L["err"] > L["epoch"] and L["total"] > L["err"]
