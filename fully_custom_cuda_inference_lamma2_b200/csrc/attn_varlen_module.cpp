@@ -518,11 +518,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "needed only after a device timeout");
     m.def(
         "set_tuning",
-        [](int64_t stages, int64_t ctas, int64_t max_cluster, int64_t solo_tiles) {
+        [](int64_t stages, int64_t ctas, int64_t max_cluster, int64_t solo_tiles, int64_t min_tiles) {
             check_rc(fcci_decode_set_tuning((int)stages, (int)ctas), "set_tuning");
-            check_rc(fcci_decode_set_cluster_limit((int)max_cluster, (int)solo_tiles), "set_tuning");
+            check_rc(fcci_decode_set_cluster_tuning((int)max_cluster, (int)solo_tiles, (int)min_tiles), "set_tuning");
         },
         "Measurement hook: pipeline stages, CTAs per SM, the largest cluster of the split mode (0 = automatic, "
         "max_cluster 1 = no clusters) and the tiles up to which a pair is not split in a cluster (-1 = automatic)",
-        py::arg("stages") = 0, py::arg("ctas_per_sm") = 0, py::arg("max_cluster") = 0, py::arg("solo_tiles") = -1);
+        py::arg("stages") = 0, py::arg("ctas_per_sm") = 0, py::arg("max_cluster") = 0, py::arg("solo_tiles") = -1,
+        py::arg("min_tiles") = 0);
 }

@@ -113,11 +113,12 @@ int fcci_decode_set_tuning(int stages, int ctas_per_sm) {
     return fcci::set_status(FCCI_OK, nullptr);
 }
 
-int fcci_decode_set_cluster_limit(int max_cluster, int solo_tiles) {
-    if (max_cluster < 0 || max_cluster > 16 || solo_tiles < -1)
-        return fcci::set_status(FCCI_EINVAL, "fcci_decode_set_cluster_limit: out of range");
+int fcci_decode_set_cluster_tuning(int max_cluster, int solo_tiles, int min_tiles) {
+    if (max_cluster < 0 || max_cluster > 16 || solo_tiles < -1 || min_tiles < 0)
+        return fcci::set_status(FCCI_EINVAL, "fcci_decode_set_cluster_tuning: out of range");
     fcci::tuning().max_cluster = max_cluster;
     fcci::tuning().solo_tiles = solo_tiles;
+    fcci::tuning().cluster_min_tiles = min_tiles;
     return fcci::set_status(FCCI_OK, nullptr);
 }
 

@@ -65,6 +65,7 @@ constexpr int kHalfTileBytes = kTileKeys * 128;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any healthy wait
 constexpr int kMaxCluster = 16;  // CTAs per cluster of a cluster launch (non-portable above 8)
 constexpr int kSoloTiles = 2;     // pairs of at most this many tiles are not split in a cluster launch
+constexpr int kClusterMinTiles = 2;  // a cluster's CTAs each own at least this many tiles at full capacity
 constexpr uint64_t kDrainLimitNs = 500000000ull;
 constexpr int kConsumerBar = 1;
 
@@ -1178,10 +1179,11 @@ static int launch_decode_t(Params prm, const CUtensorMap& mk, const CUtensorMap&
         // a batched arena bounds every pair's tiles by its capacity: no cluster needs
         // more CTAs than that (the packed layout gives no per-sequence bound here)
         const long long cap_tiles = prm.cu_seqlens ? (long long)kMaxCluster : ((long long)prm.capacity + kTileKeys - 1) / kTileKeys;
+        const long long min_tiles = g_tuning.cluster_min_tiles > 0 ? g_tuning.cluster_min_tiles : kClusterMinTiles;
         if (maxk >= 2 && 2 * P <= (long long)grid && cap_tiles >= 2) {
             long long k = (long long)grid / P;
             if (k > maxk) k = maxk;
-            if (k > cap_tiles) k = cap_tiles;
+            if (k > cap_tiles / min_tiles) k = cap_tiles / min_tiles;
             while (k >= 2 && !clusters_fit<D, NB>((int)k, P, smem, dev, non_portable[dev])) --k;
             if (k >= 2) {
                 prm.cluster_k = (int)k;

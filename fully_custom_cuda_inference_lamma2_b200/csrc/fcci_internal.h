@@ -20,6 +20,7 @@ struct Tuning {
     int ctas_per_sm = 0;  // persistent CTAs per SM in split mode; 0 = automatic
     int max_cluster = 0;  // largest cluster of a split launch; 0 = automatic (16), 1 = no clusters
     int solo_tiles = -1;  // pairs of at most this many tiles stay on one CTA of their cluster; -1 = automatic
+    int cluster_min_tiles = 0;  // tiles per cluster CTA at full arena capacity, at least; 0 = automatic
 };
 Tuning& tuning();
 

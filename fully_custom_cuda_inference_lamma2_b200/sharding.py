@@ -114,14 +114,14 @@ class CtxExchange:
     Every rank allocates one IPC buffer (exchange_layout) and maps every other rank's.
     `decode(...)` runs this rank's decode step with `out` = its slice of its own full-ctx
     buffer for the layer, and the kernel stores the same slice into every peer's buffer
-    (plain stores over NVLink, no multicast) before its last CTA raises this rank's slot
+    (one plain store per peer over NVLink) before its last CTA raises this rank's slot
     of every flag array to the next epoch. `wait()` holds the current stream until every
     rank's slot has reached this rank's epoch (bounded: FCCI_DEV_ERR_TIMEOUT in `err`
     when it runs out). Layers alternate between two buffers, so a rank that passed layer
     l's wait can store layer l+1's slice while another still reads layer l.
     Every rank must make the same calls in the same order."""
 
-    def __init__(self, B: int, Hq: int, D: int, group=None, buffers: int = 2, limit_ns: int = 1_000_000_000):
+    def __init__(self, B: int, Hq: int, D: int, group=None, buffers: int = 2, limit_ns: int = 2_000_000_000):
         import torch.distributed as dist
 
         from . import attn_varlen

@@ -196,12 +196,14 @@ int fcci_decode_read_error(void* workspace, uint32_t* flags, int clear, cudaStre
 /* Tuning hook for measurements: pipeline stages per CTA (2..8) and persistent
  * CTAs per SM (1..2) of the split mode; 0 selects the automatic choice. */
 int fcci_decode_set_tuning(int stages, int ctas_per_sm);
-/* Measurement hook: largest thread-block cluster of the split mode's cluster launch
- * (one cluster per (sequence, kv head) pair when there are at most half as many pairs
- * as resident CTAs); 0 selects the automatic limit (16), 1 turns clusters off. In such
- * a launch pairs of at most solo_tiles 64-key tiles are carried by one CTA of their
- * cluster instead of being split; -1 selects the automatic threshold. */
-int fcci_decode_set_cluster_limit(int max_cluster, int solo_tiles);
+/* Measurement hook for the split mode's cluster launch (one cluster per (sequence, kv
+ * head) pair when there are at most half as many pairs as resident CTAs):
+ *   max_cluster  largest cluster; 0 = automatic (16), 1 = no clusters
+ *   solo_tiles   pairs of at most this many 64-key tiles are carried by one CTA of
+ *                their cluster instead of being split; -1 = automatic
+ *   min_tiles    with a batched arena, each CTA of a cluster owns at least this many
+ *                tiles when a pair fills the arena's capacity; 0 = automatic */
+int fcci_decode_set_cluster_tuning(int max_cluster, int solo_tiles, int min_tiles);
 
 /* Status of the last call on this host thread, and its message. */
 int fcci_last_status(void);

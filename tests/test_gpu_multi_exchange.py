@@ -1,8 +1,8 @@
 """The ctx exchange fused into the decode launch, on 2 to 4 GPUs of one node.
 
 Each rank owns a kv-head shard; its decode launch stores the rank's ctx slice into
-every rank's full-ctx buffer over NVLink (plain stores to CUDA IPC mappings, no
-multicast) and raises a per-rank flag; sharding.CtxExchange.wait() holds the stream
+every rank's full-ctx buffer over NVLink (one plain store per peer, to CUDA IPC
+mappings) and raises a per-rank flag; sharding.CtxExchange.wait() holds the stream
 until every rank's slice has landed. Every rank's full ctx must match the fp32 oracle
 of the unsharded step (max-abs 2e-3, relative-L2 1e-3) for three layers in a row
 (alternating buffers), eagerly and replayed from a CUDA graph, with no timeout bit.
