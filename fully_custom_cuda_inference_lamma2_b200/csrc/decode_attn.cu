@@ -156,6 +156,8 @@ __device__ __forceinline__ void store_ctx1(const Params& p, int64_t off, __half 
         if (i < p.n_peers) p.peer_out[i][off] = v;
 }
 
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 __device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
@@ -902,7 +904,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     // ---- ctx exchange: every thread's stores to the peers become visible system-wide
     //      before its CTA counts in below
     if (p.n_peers > 0) {
-        __threadfence_system();
+        fence_acq_rel_sys();
         __syncthreads();
     }
     // ---- the last CTA: device-side seq_len advance (once every CTA has read the
@@ -926,7 +928,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 if (p.n_peers > 0) {
                     const uint32_t e = *p.xepoch + 1u;
                     *p.xepoch = e;
-                    __threadfence_system();
+                    fence_acq_rel_sys();
 #pragma unroll
                     for (int i = 0; i < FCCI_MAX_PEERS; ++i)
                         if (i < p.n_peers) st_release_sys(p.peer_flags[i] + p.xrank, e);

@@ -20,9 +20,15 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Thread i < n waits until flags[i] has reached the epoch (wrap-safe comparison),
-// giving up after limit_ns with the timeout bit set in *err.
+// giving up after limit_ns with the timeout bit set in *err. Launched as a
+// programmatic dependent of the decode launch before it: it is resident before that
+// launch ends and reads the epoch only after it (griddepcontrol.wait); the next
+// launch may set up in its turn while this one waits (its reads of the exchanged
+// ctx come after its own griddepcontrol.wait, i.e. after this kernel).
 __global__ void exchange_wait_kernel(const uint32_t* flags, int n, const uint32_t* epoch, uint32_t* err,
                                      uint64_t limit_ns) {
+    griddep_launch_dependents();
+    griddep_wait();
     const uint32_t e = *epoch;
     if ((int)threadIdx.x < n) {
         const uint64_t t0 = global_timer_ns();
@@ -81,9 +87,8 @@ int fcci_exchange_wait(const uint32_t* flags, int n, const uint32_t* epoch, uint
         return fcci::set_status(FCCI_EINVAL, "fcci_exchange_wait: bad argument");
     if (limit_ns == 0 || limit_ns > 10000000000ull)
         return fcci::set_status(FCCI_EINVAL, "fcci_exchange_wait: limit must be in (0, 10 s]");
-    fcci::exchange_wait_kernel<<<1, 32, 0, stream>>>(flags, n, epoch, err, limit_ns);
-    fcci::count_launch();
-    return fcci::set_cuda_status(cudaGetLastError());
+    return fcci::launch_pdl(fcci::exchange_wait_kernel, dim3(1), dim3(32), 0, stream, flags, n, epoch, err,
+                            limit_ns);
 }
 
 int fcci_decode_attention_exchange(const fcci_decode_desc* desc, const fcci_ctx_exchange* ex, cudaStream_t stream) {
