@@ -1275,6 +1275,8 @@ def main():
                     help="largest thread-block cluster of the split decode launch (0 automatic, 1 none)")
     ap.add_argument("--solo-tiles", type=int, default=-1,
                     help="pairs of at most this many tiles are not split in a cluster launch (-1 automatic)")
+    ap.add_argument("--stages", type=int, default=0, help="decode pipeline stages per CTA (0 automatic)")
+    ap.add_argument("--ctas-per-sm", type=int, default=0, help="decode split-mode CTAs per SM (0 automatic)")
     ap.add_argument("--cluster-min-tiles", type=int, default=0,
                     help="tiles each cluster CTA owns at full arena capacity, at least (0 automatic)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (A/B measurements)")
@@ -1284,11 +1286,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if (args.max_cluster or args.solo_tiles >= 0 or args.cluster_min_tiles) and args.impl == "ours":
+    if (args.max_cluster or args.solo_tiles >= 0 or args.cluster_min_tiles or args.stages or args.ctas_per_sm) \
+            and args.impl == "ours":
         import fully_custom_cuda_inference_lamma2_b200 as fcci
 
-        fcci.attn_varlen.set_tuning(max_cluster=args.max_cluster, solo_tiles=args.solo_tiles,
-                                    min_tiles=args.cluster_min_tiles)
+        fcci.attn_varlen.set_tuning(stages=args.stages, ctas_per_sm=args.ctas_per_sm, max_cluster=args.max_cluster,
+                                    solo_tiles=args.solo_tiles, min_tiles=args.cluster_min_tiles)
     if args.workload == "llama7b":
         (llama_reference if args.impl == "reference" else llama_ours)(args)
     elif args.workload == "prefill16":

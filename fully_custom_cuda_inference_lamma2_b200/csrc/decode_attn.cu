@@ -468,7 +468,6 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         }
     } else {
         // ============================================================ consumers
-        if (p.prefetch_kv) griddep_wait();
         const int w = warp;
         const int ctid = tid;  // 0..127
         const int g = lane >> 2, t4 = lane & 3;
@@ -485,6 +484,21 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         SeqInfo si = p.split ? SeqInfo{seqT[b], seqL[b], seqBase[b], true} : seq_info(p, b);
         int tiles = tiles_of(si.L);
         bool seg_start = true;
+        if (p.prefetch_kv) {
+            // the RoPE table of the first segment's position depends only on the lengths,
+            // which may be read early: build it before waiting for the previous launch
+            if (rot > 0 && ntiles > 0) {
+                for (int i = ctid; i < 2 * rhalf; i += kConsumerThreads) {
+                    const int k = i < rhalf ? i : i - rhalf;
+                    const float ang = rope_angle(p.rope_theta, k, rhalf, si.T);
+                    if (i < rhalf) rope_cs[k].x = cosf(ang);
+                    else rope_cs[k].y = sinf(ang);
+                }
+                cached_pos = si.T;
+                named_bar_sync(kConsumerBar, kConsumerThreads);
+            }
+            griddep_wait();
+        }
 
         for (int it = 0; it < ntiles; ++it) {
             if (seg_start) {
