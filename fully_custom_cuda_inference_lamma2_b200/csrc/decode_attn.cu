@@ -323,9 +323,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         for (int b = lo; b < hi; ++b)
             if (tiles_of(seqL[b]) * Hkv != misc[2]) same = false;
         uniform = __syncthreads_and(same) != 0;
-    } else if (tid == 0 && p.err) {
+    } else if (tid == 0) {
         const SeqInfo si = seq_info(p, blockIdx.x / Hkv);
         if (!si.ok && (blockIdx.x % Hkv) == 0) set_error(p, FCCI_DEV_ERR_CAPACITY);
+        misc[3] = si.T;  // the early read the guard below compares with
+        misc[4] = si.tok_base;
     }
     __syncthreads();
 
@@ -404,6 +406,23 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
 
     if (warp == kConsumerWarps) {
         // ============================================================ producer
+        if (lane != 0 && p.prefetch_kv) {
+            // guard of the early-read contract, off the critical path: once the previous
+            // kernel has finished, the idle lanes read the lengths (and sequence offsets)
+            // again; a value that changed since this CTA read it early means a kernel that
+            // was still running wrote it, and the step used a stale value
+            griddep_wait();
+            if (p.split) {
+                for (int bb = lane - 1; bb < B; bb += 31) {
+                    const int t_now = p.seq_lens ? p.seq_lens[bb] : p.fixed_len;
+                    const int base_now = p.cu_seqlens ? p.cu_seqlens[bb] : 0;
+                    if (t_now != seqT[bb] || base_now != seqBase[bb]) set_error(p, FCCI_DEV_ERR_EARLY_READ);
+                }
+            } else if (lane == 1) {
+                const SeqInfo now = seq_info(p, blockIdx.x / Hkv);
+                if (now.T != misc[3] || now.tok_base != misc[4]) set_error(p, FCCI_DEV_ERR_EARLY_READ);
+            }
+        }
         if (lane == 0 && ntiles > 0) {
             const uint64_t pol = l2_policy_evict_first();
             int b = b0, h = h0, j = j0;

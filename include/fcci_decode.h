@@ -71,6 +71,9 @@ extern "C" {
 /* device error word bits (fcci_decode_read_error) */
 #define FCCI_DEV_ERR_CAPACITY 1u /* T (+1 when appending) exceeded a sequence's capacity */
 #define FCCI_DEV_ERR_TIMEOUT 2u  /* a pipeline wait hit its time limit (kernel bailed out) */
+#define FCCI_DEV_ERR_EARLY_READ 4u /* FCCI_DECODE_PREFETCH_KV: a length or sequence offset read before the
+                                      programmatic-launch wait had changed by the end of the wait (a kernel
+                                      still running wrote it); the step used the stale value */
 
 /*
  * One decode-attention step over B sequences.
@@ -115,6 +118,10 @@ extern "C" {
  * chain of decode steps over different layers' arenas where only the last one
  * advances seq_lens (and the next step starts with a copy or a non-dependent
  * launch), or a decode step right after the projection that produced q/k/v.
+ * The kernel checks the lengths and sequence offsets it read early against their
+ * values after the wait and reports a difference as FCCI_DEV_ERR_EARLY_READ in the
+ * workspace's error word (the step's results are then not to be used). A changed
+ * arena row is not detected.
  */
 #define FCCI_DECODE_PREFETCH_KV 1u
 typedef struct fcci_decode_desc {

@@ -291,6 +291,42 @@ def test_decode_cluster_short_pairs(av, T):
     assert got["lens"].tolist() == [T + 1] * B
 
 
+@pytest.mark.parametrize("split", [True, False])
+def test_early_read_guard_reports_a_broken_contract(av, split):
+    """FCCI_DECODE_PREFETCH_KV lets a launch read the lengths before the kernel ahead of it on
+    the stream has finished; the caller promises that no such kernel writes them. Here the
+    kernel ahead breaks that promise on purpose: a decode step that advances the very lengths
+    the next (early-reading) step uses. Whatever the timing, the second step must never be
+    silently wrong: if its ctx differs from the step at the advanced lengths, its error word
+    carries FCCI_DEV_ERR_EARLY_READ (4); without the bit, its ctx is the right one."""
+    B, Hkv, G, D, T = 32, 8, 8, 128, 1000
+    qa, kna, vna, kca, vca, lens, _ = make_case(B, Hkv, G, D, [T] * B, T + 8, seed=1200)
+    qb = randn_half((B, Hkv * G, D), 1210)
+    kcb, vcb = randn_half((B, Hkv, T + 8, D), 1211), randn_half((B, Hkv, T + 8, D), 1212)
+    want = O.decode_step(qb, kcb, vcb, torch.tensor([T + 1] * B, dtype=torch.int32))["ctx"]
+    dqa, dkna, dvna, dqb = qa.to(DEV), kna.to(DEV), vna.to(DEV), qb.to(DEV)
+    dkcb, dvcb = kcb.to(DEV), vcb.to(DEV)
+    flagged = 0
+    for trial in range(8):
+        dka, dva = kca.to(DEV), vca.to(DEV)
+        seq = lens.to(DEV)
+        wsa, wsb = av.make_workspace(B, Hkv * G, Hkv, D), av.make_workspace(B, Hkv * G, Hkv, D)
+        out_a = torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV)
+        out_b = torch.full((B, Hkv * G, D), float("nan"), dtype=torch.float16, device=DEV)
+        torch.cuda.synchronize()
+        av.decode(dqa, dka, dva, out_a, k_new=dkna, v_new=dvna, seq_lens=seq, advance=True, workspace=wsa,
+                  split=True)
+        av.decode(dqb, dkcb, dvcb, out_b, seq_lens=seq, workspace=wsb, split=split, prefetch_kv=True)
+        torch.cuda.synchronize()
+        err = av.read_error(wsb)
+        max_abs, rel = O.compare(out_b.float().cpu(), want)
+        right = max_abs <= O.MAX_ABS_TOL and rel <= O.REL_L2_TOL
+        assert right or (err & 4), f"trial {trial}: stale lengths used silently (max_abs={max_abs:.3g})"
+        flagged += bool(err & 4)
+        assert seq.cpu().tolist() == [T + 1] * B
+    print(f"split={split}: {flagged} of 8 steps read stale lengths and reported it")
+
+
 def test_decode_capacity_overflow_sets_error(av):
     lens = [10, 400, 20]  # 400 + 1 > cap 400
     B, Hkv, G, D, cap = 3, 2, 4, 128, 400

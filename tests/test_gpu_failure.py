@@ -4,6 +4,7 @@ arrives on, reports the timeout bit, the kernel returns, and the same context th
 runs a decode step correctly."""
 import ctypes
 import math
+import time
 
 import pytest
 import torch
@@ -38,3 +39,28 @@ def test_bounded_wait_times_out_and_context_stays_usable():
     want = O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn, scale=1 / math.sqrt(128))
     max_abs, rel = O.compare(out.float().cpu(), want["ctx"])
     assert max_abs <= O.MAX_ABS_TOL and rel <= O.REL_L2_TOL
+
+
+def test_exchange_wait_times_out_and_reports():
+    """The ctx exchange's wait on one GPU with flags that nothing raises: the one-CTA wait
+    kernel gives up after its limit, sets FCCI_DEV_ERR_TIMEOUT (2) in the exchange's error
+    word and returns; the context stays usable (a decode step afterwards is correct)."""
+    import fully_custom_cuda_inference_lamma2_b200 as pkg
+
+    av = pkg.attn_varlen
+    mem, _ = av.ipc_alloc(1024)
+    flags, epoch, err = mem[0:16], mem[256:260], mem[512:516]
+    epoch.view(torch.int32).fill_(1)  # every flag is 0: the epoch is never reached
+    t0 = time.time()
+    av.exchange_wait(flags, 4, epoch, err, 50_000_000)  # 50 ms
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert int(err.view(torch.int32).item()) & 2
+    assert 0.04 < waited < 5.0
+    # the context still works
+    q = torch.randn(1, 8, 128, device="cuda").half()
+    kc = torch.randn(1, 1, 100, 128, device="cuda").half()
+    out = torch.empty_like(q)
+    av.decode(q, kc, kc, out, fixed_len=100, split=False)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
