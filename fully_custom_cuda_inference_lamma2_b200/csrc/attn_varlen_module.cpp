@@ -95,6 +95,7 @@ void decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor out
             c10::optional<at::Tensor> v_new, c10::optional<at::Tensor> seq_lens, c10::optional<at::Tensor> cu_seqlens,
             int64_t fixed_len, double scale, double rope_theta, int64_t rotary_dim, bool advance,
             c10::optional<at::Tensor> workspace, c10::optional<at::Tensor> q_rot_out, bool split, bool prefetch_kv,
+            bool check_early_read,
             const std::vector<uint64_t>& peer_out, const std::vector<uint64_t>& peer_flags, uint64_t exch_flags,
             uint64_t exch_epoch, int64_t exch_rank) {
     check_half_cuda(q, "q");
@@ -195,7 +196,7 @@ void decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor out
     else if (split || advance || exch_rank >= 0) ws = cached_workspace(B, Hq, Hkv, D, q.device());
     if (ws.defined()) bind_workspace(d, ws);
     d.split = split ? 1 : 0;
-    d.flags = prefetch_kv ? FCCI_DECODE_PREFETCH_KV : 0u;
+    d.flags = (prefetch_kv ? FCCI_DECODE_PREFETCH_KV : 0u) | (check_early_read ? FCCI_DECODE_CHECK_EARLY_READ : 0u);
     if (exch_rank >= 0) {
         // ctx exchange: `out` is this rank's slice of its full-ctx buffer; the peers'
         // mappings receive the same slice at the same offsets
@@ -419,6 +420,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("fixed_len") = -1, py::arg("scale") = -1.0, py::arg("rope_theta") = 10000.0,
           py::arg("rotary_dim") = -1, py::arg("advance") = false, py::arg("workspace") = py::none(),
           py::arg("q_rot_out") = py::none(), py::arg("split") = true, py::arg("prefetch_kv") = false, py::kw_only(),
+          py::arg("check_early_read") = false,
           py::arg("peer_out") = std::vector<uint64_t>(), py::arg("peer_flags") = std::vector<uint64_t>(),
           py::arg("exch_flags") = 0, py::arg("exch_epoch") = 0, py::arg("exch_rank") = -1);
     m.def("rope_append", &rope_append, "RoPE(q,k_new) at T and append of k/v at T (no attention)", py::arg("q"),

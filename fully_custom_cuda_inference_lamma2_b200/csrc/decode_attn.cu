@@ -94,6 +94,7 @@ struct Params {
     int32_t append;
     int32_t split;
     int32_t prefetch_kv;  // FCCI_DECODE_PREFETCH_KV: lengths and the first stages before griddepcontrol.wait
+    int32_t check_early;  // FCCI_DECODE_CHECK_EARLY_READ: launch the instantiation with the early-read guard
     int32_t cluster_k;    // CTAs per cluster of a split launch in clusters of one pair each; 0 otherwise
     int32_t solo_tiles;   // in such a launch, pairs of at most this many tiles stay on one CTA
     // ctx exchange (fcci_exchange.h): the slice also goes to n_peers peers' buffers at the
@@ -220,7 +221,9 @@ struct Layout {
     }
 };
 
-template <int D, int NB>
+// CHECK: the opt-in guard of the early-read contract (FCCI_DECODE_CHECK_EARLY_READ) is
+// compiled in; the default instantiation carries none of its code.
+template <int D, int NB, bool CHECK>
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                const __grid_constant__ CUtensorMap tmV,
                                                                const __grid_constant__ CUtensorMap tmK64,
@@ -406,23 +409,6 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
 
     if (warp == kConsumerWarps) {
         // ============================================================ producer
-        if (lane != 0 && p.prefetch_kv) {
-            // guard of the early-read contract, off the critical path: once the previous
-            // kernel has finished, the idle lanes read the lengths (and sequence offsets)
-            // again; a value that changed since this CTA read it early means a kernel that
-            // was still running wrote it, and the step used a stale value
-            griddep_wait();
-            if (p.split) {
-                for (int bb = lane - 1; bb < B; bb += 31) {
-                    const int t_now = p.seq_lens ? p.seq_lens[bb] : p.fixed_len;
-                    const int base_now = p.cu_seqlens ? p.cu_seqlens[bb] : 0;
-                    if (t_now != seqT[bb] || base_now != seqBase[bb]) set_error(p, FCCI_DEV_ERR_EARLY_READ);
-                }
-            } else if (lane == 1) {
-                const SeqInfo now = seq_info(p, blockIdx.x / Hkv);
-                if (now.T != misc[3] || now.tok_base != misc[4]) set_error(p, FCCI_DEV_ERR_EARLY_READ);
-            }
-        }
         if (lane == 0 && ntiles > 0) {
             const uint64_t pol = l2_policy_evict_first();
             int b = b0, h = h0, j = j0;
@@ -503,6 +489,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
         SeqInfo si = p.split ? SeqInfo{seqT[b], seqL[b], seqBase[b], true} : seq_info(p, b);
         int tiles = tiles_of(si.L);
         bool seg_start = true;
+        int guard_t = 0, guard_base = 0;
         if (p.prefetch_kv) {
             // the RoPE table of the first segment's position depends only on the lengths,
             // which may be read early: build it before waiting for the previous launch
@@ -517,6 +504,20 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 named_bar_sync(kConsumerBar, kConsumerThreads);
             }
             griddep_wait();
+            // guard of the early-read contract (opt-in): read the lengths (and sequence
+            // offsets) again now that the previous kernel has finished; they are compared
+            // with the early values at the end of the kernel
+            if (!CHECK) {
+            } else if (p.split) {
+                if (ctid < B) {
+                    guard_t = p.seq_lens ? p.seq_lens[ctid] : p.fixed_len;
+                    guard_base = p.cu_seqlens ? p.cu_seqlens[ctid] : 0;
+                }
+            } else if (ctid == 0) {
+                const SeqInfo now = seq_info(p, blockIdx.x / Hkv);
+                guard_t = now.T;
+                guard_base = now.tok_base;
+            }
         }
 
         for (int it = 0; it < ntiles; ++it) {
@@ -886,6 +887,22 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
                 }
             }
         }
+        if (CHECK && p.prefetch_kv) {
+            // a value that changed since this CTA read it early means a kernel that was
+            // still running wrote it, and the step used a stale value
+            bool stale = false;
+            if (p.split) {
+                if (ctid < B) stale = guard_t != seqT[ctid] || guard_base != seqBase[ctid];
+                for (int bb = ctid + kConsumerThreads; bb < B; bb += kConsumerThreads) {
+                    const int t_now = p.seq_lens ? p.seq_lens[bb] : p.fixed_len;
+                    const int base_now = p.cu_seqlens ? p.cu_seqlens[bb] : 0;
+                    stale = stale || t_now != seqT[bb] || base_now != seqBase[bb];
+                }
+            } else if (ctid == 0) {
+                stale = guard_t != misc[3] || guard_base != misc[4];
+            }
+            if (stale) set_error(p, FCCI_DEV_ERR_EARLY_READ);
+        }
     }
 
     __syncthreads();
@@ -1129,11 +1146,11 @@ int max_grid(int dev) { return device_sm_count(dev) * kMaxCtasPerSm; }
 // Can `clusters` clusters of k CTAs of this kernel (with `smem` bytes of dynamic shared
 // memory each) be resident on device `dev` at once? Answered by the occupancy API and
 // remembered per (device, k, shared memory).
-template <int D, int NB>
+template <int D, int NB, bool CHECK>
 static bool clusters_fit(int k, long long clusters, size_t smem, int dev, bool non_portable_ok) {
     if (k > 8 && !non_portable_ok) return false;
     static std::mutex mu;
-    static std::map<std::tuple<int, int, size_t>, int> cache;
+    static std::map<std::tuple<int, int, size_t>, int> cache;  // one per instantiation
     const auto key = std::make_tuple(dev, k, smem);
     int n = -1;
     {
@@ -1153,7 +1170,7 @@ static bool clusters_fit(int k, long long clusters, size_t smem, int dev, bool n
         a[0].val.clusterDim.z = 1;
         cfg.attrs = a;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<D, NB>, &cfg) != cudaSuccess) {
+        if (cudaOccupancyMaxActiveClusters(&n, decode_attn_kernel<D, NB, CHECK>, &cfg) != cudaSuccess) {
             cudaGetLastError();
             n = 0;
         }
@@ -1163,7 +1180,7 @@ static bool clusters_fit(int k, long long clusters, size_t smem, int dev, bool n
     return (long long)n >= clusters;
 }
 
-template <int D, int NB>
+template <int D, int NB, bool CHECK>
 static int launch_decode_t(Params prm, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mk64,
                            const CUtensorMap& mv64, int grid, cudaStream_t st,
                            int dev) {
@@ -1173,11 +1190,11 @@ static int launch_decode_t(Params prm, const CUtensorMap& mk, const CUtensorMap&
     static bool non_portable[128];
     if (dev < 0 || dev >= 128) return FCCI_EINVAL;
     std::call_once(flags[dev], [&]() {
-        attr_err[dev] = cudaFuncSetAttribute(decode_attn_kernel<D, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_err[dev] = cudaFuncSetAttribute(decode_attn_kernel<D, NB, CHECK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              227 * 1024);
         // clusters of more than 8 CTAs need this opt-in; without it they are not used
         non_portable[dev] =
-            cudaFuncSetAttribute(decode_attn_kernel<D, NB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+            cudaFuncSetAttribute(decode_attn_kernel<D, NB, CHECK>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
             cudaSuccess;
         if (!non_portable[dev]) cudaGetLastError();
     });
@@ -1196,7 +1213,7 @@ static int launch_decode_t(Params prm, const CUtensorMap& mk, const CUtensorMap&
             if (occ_val[dev] > 0 && occ_smem[dev] == smem) occ = occ_val[dev];
         }
         if (occ == 0) {
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_attn_kernel<D, NB>, kThreads, smem) !=
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_attn_kernel<D, NB, CHECK>, kThreads, smem) !=
                 cudaSuccess) {
                 cudaGetLastError();
                 occ = 0;
@@ -1219,7 +1236,7 @@ static int launch_decode_t(Params prm, const CUtensorMap& mk, const CUtensorMap&
             long long k = (long long)grid / P;
             if (k > maxk) k = maxk;
             if (k > cap_tiles / min_tiles) k = cap_tiles / min_tiles;
-            while (k >= 2 && !clusters_fit<D, NB>((int)k, P, smem, dev, non_portable[dev])) --k;
+            while (k >= 2 && !clusters_fit<D, NB, CHECK>((int)k, P, smem, dev, non_portable[dev])) --k;
             if (k >= 2) {
                 prm.cluster_k = (int)k;
                 prm.solo_tiles = g_tuning.solo_tiles >= 0 ? g_tuning.solo_tiles : kSoloTiles;
@@ -1227,7 +1244,7 @@ static int launch_decode_t(Params prm, const CUtensorMap& mk, const CUtensorMap&
             }
         }
     }
-    return launch_pdl_cluster(decode_attn_kernel<D, NB>, dim3(grid), dim3(kThreads), smem, st, prm.cluster_k, mk, mv,
+    return launch_pdl_cluster(decode_attn_kernel<D, NB, CHECK>, dim3(grid), dim3(kThreads), smem, st, prm.cluster_k, mk, mv,
                               mk64, mv64, prm);
 }
 
@@ -1272,7 +1289,7 @@ static int fill_params(const fcci_decode_desc* d, Params& p, bool attention) {
     if (d->abi_version != 1 && d->abi_version != FCCI_DECODE_ABI_VERSION)
         return bad(FCCI_EINVAL, "abi_version mismatch");
     const uint32_t flags = d->abi_version >= 2 ? d->flags : 0u;
-    if (flags & ~FCCI_DECODE_PREFETCH_KV) return bad(FCCI_EINVAL, "unknown bits in flags");
+    if (flags & ~(FCCI_DECODE_PREFETCH_KV | FCCI_DECODE_CHECK_EARLY_READ)) return bad(FCCI_EINVAL, "unknown bits in flags");
     if (d->B <= 0 || d->Hq <= 0 || d->Hkv <= 0 || d->Hq % d->Hkv != 0)
         return bad(FCCI_EINVAL, "B, Hq, Hkv must be positive and Hq a multiple of Hkv");
     if (d->D != 64 && d->D != 128 && d->D != 256) return bad(FCCI_EUNSUPPORTED, "unsupported head_dim (64, 128 or 256)");
@@ -1336,6 +1353,7 @@ static int fill_params(const fcci_decode_desc* d, Params& p, bool attention) {
     p.append = d->k_new ? 1 : 0;
     p.split = d->split ? 1 : 0;
     p.prefetch_kv = (flags & FCCI_DECODE_PREFETCH_KV) ? 1 : 0;
+    p.check_early = (flags & FCCI_DECODE_CHECK_EARLY_READ) ? 1 : 0;
     p.B = d->B;
     p.Hq = d->Hq;
     p.Hkv = d->Hkv;
@@ -1407,12 +1425,18 @@ int decode_attention(const fcci_decode_desc* d, cudaStream_t stream, const fcci_
     if (!rc) rc = encode_kv_map(&mv64, p.v_cache, d->D, p.capacity, p.Hkv, Bdim, p.v_st, p.v_sh, p.v_sb, kTileKeys);
     if (rc) return set_status(rc, "fcci_decode_attention: cuTensorMapEncodeTiled rejected the arena layout");
 
+    const bool check = p.check_early && p.prefetch_kv;
     switch (d->D * 10 + NB) {
-        case 641: return launch_decode_t<64, 1>(p, mk, mv, mk64, mv64, grid, stream, dev);
-        case 642: return launch_decode_t<64, 2>(p, mk, mv, mk64, mv64, grid, stream, dev);
-        case 1281: return launch_decode_t<128, 1>(p, mk, mv, mk64, mv64, grid, stream, dev);
-        case 1282: return launch_decode_t<128, 2>(p, mk, mv, mk64, mv64, grid, stream, dev);
-        case 2561: return launch_decode_t<256, 1>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 641: return check ? launch_decode_t<64, 1, true>(p, mk, mv, mk64, mv64, grid, stream, dev)
+                               : launch_decode_t<64, 1, false>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 642: return check ? launch_decode_t<64, 2, true>(p, mk, mv, mk64, mv64, grid, stream, dev)
+                               : launch_decode_t<64, 2, false>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 1281: return check ? launch_decode_t<128, 1, true>(p, mk, mv, mk64, mv64, grid, stream, dev)
+                                : launch_decode_t<128, 1, false>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 1282: return check ? launch_decode_t<128, 2, true>(p, mk, mv, mk64, mv64, grid, stream, dev)
+                                : launch_decode_t<128, 2, false>(p, mk, mv, mk64, mv64, grid, stream, dev);
+        case 2561: return check ? launch_decode_t<256, 1, true>(p, mk, mv, mk64, mv64, grid, stream, dev)
+                                : launch_decode_t<256, 1, false>(p, mk, mv, mk64, mv64, grid, stream, dev);
         default: return set_status(FCCI_EUNSUPPORTED, "fcci_decode_attention: unsupported head_dim");
     }
 }

@@ -118,12 +118,16 @@ extern "C" {
  * chain of decode steps over different layers' arenas where only the last one
  * advances seq_lens (and the next step starts with a copy or a non-dependent
  * launch), or a decode step right after the projection that produced q/k/v.
- * The kernel checks the lengths and sequence offsets it read early against their
- * values after the wait and reports a difference as FCCI_DEV_ERR_EARLY_READ in the
- * workspace's error word (the step's results are then not to be used). A changed
- * arena row is not detected.
+ *
+ * FCCI_DECODE_CHECK_EARLY_READ (with FCCI_DECODE_PREFETCH_KV): the kernel also reads
+ * the lengths and sequence offsets again after the wait and reports any that changed
+ * since its early read as FCCI_DEV_ERR_EARLY_READ in the workspace's error word (the
+ * step's results are then not to be used). A changed arena row is not detected. It
+ * costs about half a microsecond per launch, so it is meant for validating a caller's
+ * use of the early reads, not for every step.
  */
 #define FCCI_DECODE_PREFETCH_KV 1u
+#define FCCI_DECODE_CHECK_EARLY_READ 2u
 typedef struct fcci_decode_desc {
     int32_t abi_version; /* FCCI_DECODE_ABI_VERSION */
     int32_t B, Hq, Hkv, D;

@@ -9,6 +9,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(ROOT, "fully_custom_cuda_inference_lamma2_b200", "libfcci_decode.so")
 ABI_VERSION = 2
 PREFETCH_KV = 1
+CHECK_EARLY_READ = 2
 
 c_i32, c_i64, c_vp, c_f32, c_sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t
 

@@ -296,9 +296,10 @@ def test_early_read_guard_reports_a_broken_contract(av, split):
     """FCCI_DECODE_PREFETCH_KV lets a launch read the lengths before the kernel ahead of it on
     the stream has finished; the caller promises that no such kernel writes them. Here the
     kernel ahead breaks that promise on purpose: a decode step that advances the very lengths
-    the next (early-reading) step uses. Whatever the timing, the second step must never be
-    silently wrong: if its ctx differs from the step at the advanced lengths, its error word
-    carries FCCI_DEV_ERR_EARLY_READ (4); without the bit, its ctx is the right one."""
+    the next (early-reading) step uses. With the check on (FCCI_DECODE_CHECK_EARLY_READ),
+    whatever the timing, the second step must never be silently wrong: if its ctx differs
+    from the step at the advanced lengths, its error word carries FCCI_DEV_ERR_EARLY_READ (4);
+    without the bit, its ctx is the right one."""
     B, Hkv, G, D, T = 32, 8, 8, 128, 1000
     qa, kna, vna, kca, vca, lens, _ = make_case(B, Hkv, G, D, [T] * B, T + 8, seed=1200)
     qb = randn_half((B, Hkv * G, D), 1210)
@@ -316,7 +317,8 @@ def test_early_read_guard_reports_a_broken_contract(av, split):
         torch.cuda.synchronize()
         av.decode(dqa, dka, dva, out_a, k_new=dkna, v_new=dvna, seq_lens=seq, advance=True, workspace=wsa,
                   split=True)
-        av.decode(dqb, dkcb, dvcb, out_b, seq_lens=seq, workspace=wsb, split=split, prefetch_kv=True)
+        av.decode(dqb, dkcb, dvcb, out_b, seq_lens=seq, workspace=wsb, split=split, prefetch_kv=True,
+                  check_early_read=True)
         torch.cuda.synchronize()
         err = av.read_error(wsb)
         max_abs, rel = O.compare(out_b.float().cpu(), want)
