@@ -1075,7 +1075,7 @@ def llama_ours(args):
                    "l2": "no flush: 13.2 GB of weights per step > 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": hbm_src, "traffic": None,
-                     "kernel": "whole token step (cuBLAS GEMVs + decode_attn_kernel + RMSNorm/SwiGLU)",
+                     "kernel": "whole token step (fused gemv_kernel projections + decode_attn_kernel; RMSNorm/SwiGLU/residual fused)",
                      "algorithmic_bytes_per_step": step_bytes, "avg_step_ms": round(ms / K, 5)},
         "e2e": {"value": round(e2e_steps / (e2e_ms / 1e3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 8, "api": "graph replay per token, token id host->device and back"},

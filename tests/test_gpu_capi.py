@@ -81,7 +81,8 @@ def test_descriptor_errors_are_status_codes(lib):
 
 def test_descriptor_versions_and_flags(lib):
     """A version-1 descriptor (no flags field) still works; FCCI_DECODE_PREFETCH_KV gives
-    the same bits; unknown flag bits are rejected with a status code."""
+    the same bits, with or without FCCI_DECODE_CHECK_EARLY_READ; unknown flag bits are rejected
+    with a status code."""
     B, Hkv, G, D, cap = 4, 2, 8, 128, 900
     lens = [3, 200, 880, 64]
     q, kn, vn = randn_half((B, Hkv * G, D), 20), randn_half((B, Hkv, D), 21), randn_half((B, Hkv, D), 22)
@@ -92,7 +93,7 @@ def test_descriptor_versions_and_flags(lib):
     stream = torch.cuda.current_stream().cuda_stream
     assert lib.fcci_decode_workspace_init(ws.data_ptr(), nbytes, stream) == 0
     outs = []
-    for version, flags in ((2, 0), (2, C.PREFETCH_KV), (1, 0)):
+    for version, flags in ((2, 0), (2, C.PREFETCH_KV), (2, C.PREFETCH_KV | C.CHECK_EARLY_READ), (1, 0)):
         dk, dv, dT = kc.to(DEV), vc.to(DEV), T.to(DEV)
         out = torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV)
         d = C.batched_desc(q.to(DEV), dk, dv, out, k_new=kn.to(DEV), v_new=vn.to(DEV), seq_lens=dT, advance=True,
@@ -108,10 +109,10 @@ def test_descriptor_versions_and_flags(lib):
         torch.cuda.synchronize()
         assert dT.cpu().tolist() == [t + 1 for t in lens]
         outs.append(out.cpu())
-    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
     ma, rl = close(outs[0], O.decode_step(q, kc, vc, T, k_new=kn, v_new=vn)["ctx"])
     assert ma <= O.MAX_ABS_TOL and rl <= O.REL_L2_TOL, (ma, rl)
     d = C.batched_desc(q.to(DEV), kc.to(DEV), vc.to(DEV), torch.empty(B, Hkv * G, D, dtype=torch.float16, device=DEV),
-                       fixed_len=5, workspace=ws, flags=2)
+                       fixed_len=5, workspace=ws, flags=4)
     assert lib.fcci_decode_attention(ctypes.byref(d), stream) == 1
     assert b"flags" in lib.fcci_last_error_string()

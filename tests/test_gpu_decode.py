@@ -7,6 +7,7 @@ reference evaluates it), and within 2e-3 of the CPU oracle, whose powf/cosf/sinf
 differ from the GPU's in the last fp32 bits. Appended V rows and untouched arena
 rows bit-exact.
 """
+import gc
 import math
 
 import pytest
@@ -117,16 +118,25 @@ def test_repeated_reference_calls_neither_allocate_nor_memset(av):
     cds = pkg.capture_decode_step
     cds.capture_decode(ctrl, ak, avv, sl, z32, logits, q=q, k_new=kn, v_new=vn, ctx_out=ctx, advance=False)
     torch.cuda.synchronize()
-    before = torch.cuda.memory_allocated()
-    kept = []
-    from torch.profiler import ProfilerActivity, profile
+    # Tensors of earlier tests held by reference cycles (a failed test's traceback frames)
+    # would otherwise be freed by a collection inside the measured loop.
+    gc.collect()
+    gc.disable()
+    try:
+        before = torch.cuda.memory_allocated()
+        kept = []
+        from torch.profiler import ProfilerActivity, profile
 
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        for _ in range(4):
-            kept.append(av.forward(q, k, v, T, 0.0883883))
-            cds.capture_decode(ctrl, ak, avv, sl, z32, logits, q=q, k_new=kn, v_new=vn, ctx_out=ctx, advance=False)
-        torch.cuda.synchronize()
-    assert torch.cuda.memory_allocated() - before == sum(t.numel() * 2 for t in kept)
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for _ in range(4):
+                kept.append(av.forward(q, k, v, T, 0.0883883))
+                cds.capture_decode(ctrl, ak, avv, sl, z32, logits, q=q, k_new=kn, v_new=vn, ctx_out=ctx,
+                                   advance=False)
+            torch.cuda.synchronize()
+        grown = torch.cuda.memory_allocated() - before
+    finally:
+        gc.enable()
+    assert grown == sum(t.numel() * 2 for t in kept)
     names = [e.name for e in prof.events()]
     assert any("decode_attn_kernel" in n for n in names), "profiler recorded no kernels"
     assert not any("memset" in n.lower() for n in names), "a memset ran inside the repeated calls"
