@@ -68,6 +68,22 @@ constexpr uint32_t kTableMagic = 0x52504531u;  // "RPE1"
 constexpr int kMaxSortB = 1024;                 // sequences ranked by length up to this batch size
 constexpr int kPrepThreads = 256;
 
+// Column pairs of each 32-column slice of S whose exponentials run on the FMA
+// pipe (bit i: columns 2i, 2i+1); the others use the SFU's ex2. Per key tile and
+// SM the two query tiles need as many exponentials (2 x 16384, 2048 cycles at 16
+// per cycle) as the MMAs need tensor cycles (2048). Measured on the prefill16
+// workload, moving 4, 5 or 8 of 16 pairs to the FMA pipe made the attention
+// launch 3, 3.5 and 7.6 % slower than the SFU alone (the softmax is bound by its
+// per-row instruction chain, not by the SFU), so the default is 0.
+#ifndef FCCI_PF_POLY_MASK
+#define FCCI_PF_POLY_MASK 0x0u
+#endif
+constexpr uint32_t kPolyMask = FCCI_PF_POLY_MASK;
+#ifndef FCCI_PF_REG_SPLIT
+#define FCCI_PF_REG_SPLIT 1
+#endif
+constexpr int kRegsLow = 104, kRegsHigh = 200;
+
 struct Params {
     const __half* q;
     int64_t q_st, q_sh;
@@ -151,6 +167,37 @@ __device__ __forceinline__ SeqRange seq_range(const Params& p, int b) {
          (long long)s.T + s.n <= cap;
     s.ok = ok;
     return s;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for two values x <= 8 on the FMA pipe (no SFU). Cody-Waite range reduction:
+// x = n + f with n = round(x), taken from the low bits of x + 1.5 * 2^23, and
+// f = x - n in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients were
+// fitted with the Remez exchange algorithm to the minimax relative error on
+// [-1/2, 1/2] (max 7.5e-5 in fp32 Horner form, below half an fp16 ulp: P is
+// rounded to fp16 for the PV MMA); 2^n is added into the exponent field. x is
+// clamped at -120 first so that the exponent cannot underflow (2^-120 rounds to
+// 0 in fp16 like the true value; -inf from masked columns gives 2^-120 * ~1).
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer
+    constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
+    x.x = fmaxf(x.x, -120.f);
+    x.y = fmaxf(x.y, -120.f);
+    const float2 j = __fadd2_rn(x, make_float2(kRound, kRound));
+    const float2 n = __fadd2_rn(j, make_float2(-kRound, -kRound));
+    const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+    float2 p = __ffma2_rn(make_float2(c3, c3), f, make_float2(c2, c2));
+    p = __ffma2_rn(p, f, make_float2(c1, c1));
+    p = __ffma2_rn(p, f, make_float2(c0, c0));
+    // the low 9 bits of j hold n (two's complement): shifted into the exponent
+    // field they add n to the exponent of p in [2^-1/2, 2^1/2]
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(j.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(j.y) << 23)));
 }
 
 __device__ __forceinline__ void set_error(const Params& p, uint32_t bit) {
@@ -442,6 +489,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         set_error(p, bit);
     };
 
+    // Register split per warpgroup, taken at the top of each warpgroup's branch so
+    // that the compiler allocates each branch under its own limit: the producer /
+    // MMA warpgroup (warps 0-3; warps 2-3 idle) drops to kRegsLow, the two softmax
+    // warpgroups rise to kRegsHigh. 128 x kRegsLow + 256 x kRegsHigh must not
+    // exceed the 384 x 168 registers the block is launched with, or the increase
+    // would wait for registers that never come free.
+    static_assert(128 * kRegsLow + 256 * kRegsHigh <= kThreads * 168, "register split above the launch's total");
+    if (warp < 4) {
+#if FCCI_PF_REG_SPLIT
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+#endif
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
@@ -661,7 +719,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait_bounded(drain, 0, &never, kDrainLimitNs);
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    }
+    } else {
+#if FCCI_PF_REG_SPLIT
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+#endif
         // ------------------------------------------------------------ softmax + epilogue
         const int g = (warp - 4) >> 2;
         const int r = tid - 128 * (1 + g);  // query row of this thread in tile g
@@ -707,12 +769,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int i = 0; i < 32; ++i)
                             if (32 * c + i >= vis) sr[c][i] = __float_as_uint(-INFINITY);
                 }
-                float mx = -INFINITY;
+                // row maximum: three-input max, two independent chains
+                float mxa = -INFINITY, mxb = -INFINITY;
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[c][i]));
-                mx *= sl2;
+                    for (int i = 0; i < 32; i += 4) {
+                        mxa = fmax3(mxa, __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+                        mxb = fmax3(mxb, __uint_as_float(sr[c][i + 2]), __uint_as_float(sr[c][i + 3]));
+                    }
+                float mx = fmaxf(mxa, mxb) * sl2;
                 float alpha = 1.f;
                 const bool resc = mx > m + kRescaleLog2;
                 if (resc) {
@@ -721,20 +787,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                     l *= alpha;
                 }
                 const float mu = (m == -INFINITY) ? 0.f : m;
-                float rs = 0.f;
-                // P = 2^(s * scale * log2 e - m) as fp16 over the first 64 columns of S_g
+                const float2 scl = make_float2(sl2, sl2), nmu = make_float2(-mu, -mu);
+                float2 rsa = make_float2(0.f, 0.f), rsb = make_float2(0.f, 0.f);
+                // P = 2^(s * scale * log2 e - m) as fp16 over the first 64 columns of S_g;
+                // column pairs in kPolyMask on the FMA pipe, the rest on the SFU
 #pragma unroll
                 for (int q4 = 0; q4 < 4; ++q4) {
                     uint32_t pk[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const float p0 = ex2(fmaf(__uint_as_float(sr[q4][2 * i]), sl2, -mu));
-                        const float p1 = ex2(fmaf(__uint_as_float(sr[q4][2 * i + 1]), sl2, -mu));
-                        rs += p0 + p1;
-                        pk[i] = pack_half2(p0, p1);
+                        const float2 x = __ffma2_rn(
+                            make_float2(__uint_as_float(sr[q4][2 * i]), __uint_as_float(sr[q4][2 * i + 1])), scl, nmu);
+                        const float2 e = ((kPolyMask >> i) & 1u) ? exp2_fma2(x) : make_float2(ex2(x.x), ex2(x.y));
+                        if (i & 1)
+                            rsb = __fadd2_rn(rsb, e);
+                        else
+                            rsa = __fadd2_rn(rsa, e);
+                        pk[i] = pack_half2(e.x, e.y);
                     }
                     tc::st16(s_addr + 16 * q4, pk);
                 }
+                const float rs = (rsa.x + rsa.y) + (rsb.x + rsb.y);
                 // rows whose maximum moved rescale O_g (idle: PV_g of the previous
                 // tile completed before S_g of this one was signalled)
                 if (j > 0 && __any_sync(0xffffffffu, resc)) {
