@@ -60,6 +60,11 @@ constexpr int kTileRows = 128;
 constexpr int kPairRows = 256;
 constexpr int kTileBytes = kTileRows * D * 2;  // 32 KB: 128 rows x 128 fp16
 constexpr int kHalfBytes = kTileBytes / 2;     // one 64-column block
+// K tiles in flight: 2 (K_j + 1 is read one tile ahead of the PV of tile j). V tiles: 3. A
+// V stage is released only when the PV MMAs of its tile complete, so with two stages
+// V_{j+2} started loading about one tile period before the MMA warp needed it, and
+// the MMA warp waited for it (an L2-latency stall on every tile).
+constexpr int kVStages = 3;
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any healthy wait
 constexpr uint64_t kDrainLimitNs = 500000000ull;
@@ -406,14 +411,16 @@ __device__ __forceinline__ int ntiles_of(const Item& it, int g) {
 }
 
 struct Smem {
-    // tiles (each 1024-byte aligned): Q0 Q1 | K0 K1 | V0 V1
+    // tiles (each 1024-byte aligned): Q0 Q1 | K0 K1 | V stages
     static constexpr int kQ = 0;
     static constexpr int kK = 2 * kTileBytes;
     static constexpr int kV = 4 * kTileBytes;
-    static constexpr int kBars = 6 * kTileBytes;
+    static constexpr int kBars = (4 + kVStages) * kTileBytes;
     // barriers (uint64 each)
-    static constexpr int kQFull = 0, kQEmpty = 2, kKFull = 4, kKEmpty = 6, kVFull = 8, kVEmpty = 10, kSFull = 12,
-                         kPFull = 14, kOFull = 16, kItemFull = 18, kItemEmpty = 20, kDrain = 22, kNumBars = 23;
+    static constexpr int kQFull = 0, kQEmpty = 2, kKFull = 4, kKEmpty = 6, kVFull = 8, kVEmpty = kVFull + kVStages,
+                         kSFull = kVEmpty + kVStages, kPFull = kSFull + 2, kOFull = kPFull + 2, kItemFull = kOFull + 2,
+                         kItemEmpty = kItemFull + 2, kDrain = kItemEmpty + 2, kNumBars = kDrain + 1;
+    static_assert(kNumBars * 8 <= 256, "barrier area");
     static constexpr int kRing = kBars + 256;  // 2 x Item
     static constexpr int kMisc = kRing + 64;   // tmem base, abort flag, last-CTA flag
     static constexpr int kBytes = kMisc + 64;
@@ -461,13 +468,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(q_empty + i, 1);
             mbar_init(k_full + i, 1);
             mbar_init(k_empty + i, 1);
-            mbar_init(v_full + i, 1);
-            mbar_init(v_empty + i, 1);
             mbar_init(s_full + i, 1);
             mbar_init(p_full + i, kTileRows);
             mbar_init(o_full + i, 1);
             mbar_init(item_full + i, 1);
             mbar_init(item_empty + i, 1 + 8);  // the MMA warp and the 8 softmax warps
+        }
+        for (int i = 0; i < kVStages; ++i) {
+            mbar_init(v_full + i, 1);
+            mbar_init(v_empty + i, 1);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -509,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t pol_q = l2_policy_evict_first();
             int tctr = 0;
             int nq[2] = {0, 0};
-            bool ok = true;
+            bool ok = true, kv_short = false;
             for (int it = 0; ok; ++it) {
                 const int slot = it & 1;
                 if (!wait_bar(item_empty + slot, ((it >> 1) & 1) ^ 1, abort_flag)) {
@@ -562,17 +571,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(k_full + st, kTileBytes);
                     tma_load_4d_plain(kd, &map_k, 0, row, hk, item.kvb, k_full + st);
                     tma_load_4d_plain(kd + kHalfBytes, &map_k, 64, row, hk, item.kvb, k_full + st);
-                    if (!wait_bar(v_empty + st, par, abort_flag)) {
+                    const int vs = tctr % kVStages;
+                    if (!wait_bar(v_empty + vs, ((tctr / kVStages) & 1) ^ 1, abort_flag)) {
                         fail(FCCI_DEV_ERR_TIMEOUT);
                         ok = false;
-                        // the K tile just issued is drained below
+                        // the K tile just issued is drained below (its V tile was not)
                         ++tctr;
+                        kv_short = true;
                         break;
                     }
-                    uint8_t* vd = sm + Smem::kV + st * kTileBytes;
-                    mbar_arrive_expect_tx(v_full + st, kTileBytes);
-                    tma_load_4d_plain(vd, &map_v, 0, row, hk, item.kvb, v_full + st);
-                    tma_load_4d_plain(vd + kHalfBytes, &map_v, 64, row, hk, item.kvb, v_full + st);
+                    uint8_t* vd = sm + Smem::kV + vs * kTileBytes;
+                    mbar_arrive_expect_tx(v_full + vs, kTileBytes);
+                    tma_load_4d_plain(vd, &map_v, 0, row, hk, item.kvb, v_full + vs);
+                    tma_load_4d_plain(vd + kHalfBytes, &map_v, 64, row, hk, item.kvb, v_full + vs);
                 }
             }
             if (*abort_flag) {
@@ -581,11 +592,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int g = 0; g < 2; ++g)
                     if (nq[g] > 0) mbar_wait_bounded(q_full + g, (nq[g] - 1) & 1, &never, kDrainLimitNs);
                 for (int st = 0; st < 2; ++st) {
-                    const int uses = (tctr - st + 1) / 2;  // tiles issued on stage st
-                    if (uses > 0) {
-                        mbar_wait_bounded(k_full + st, (uses - 1) & 1, &never, kDrainLimitNs);
-                        mbar_wait_bounded(v_full + st, (uses - 1) & 1, &never, kDrainLimitNs);
-                    }
+                    const int uses = (tctr - st + 1) / 2;  // K tiles issued on stage st
+                    if (uses > 0) mbar_wait_bounded(k_full + st, (uses - 1) & 1, &never, kDrainLimitNs);
+                }
+                const int vtiles = kv_short ? tctr - 1 : tctr;  // V tiles issued
+                for (int st = 0; st < kVStages; ++st) {
+                    const int uses = (vtiles - st + kVStages - 1) / kVStages;
+                    if (uses > 0) mbar_wait_bounded(v_full + st, (uses - 1) & 1, &never, kDrainLimitNs);
                 }
             }
         }
@@ -594,21 +607,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t id_qk = tc::idesc_f16_f32(128, 128, 0, 0);
         const uint32_t id_pv = tc::idesc_f16_f32(128, 128, 0, 1);
         const uint32_t sq = smem_u32(sm + Smem::kQ), sk = smem_u32(sm + Smem::kK), sv = smem_u32(sm + Smem::kV);
+        // One descriptor per operand buffer per call; a byte offset b inside the
+        // buffer adds b / 16 to the 14-bit start-address field in the low word (no
+        // carry: shared-memory addresses stay below 256 KB), so each MMA costs the
+        // issuing thread one 32-bit add per operand instead of a rebuilt descriptor.
+        // The MMA warp shares its SM sub-partition with two softmax warps; fewer
+        // instructions per MMA let it keep the tensor pipe fed.
+        auto desc_off = [](uint64_t d, uint32_t bytes) -> uint64_t {
+            return ((d >> 32) << 32) | (uint32_t)((uint32_t)d + (bytes >> 4));
+        };
         auto issue_s = [&](int g, int st) {  // S_g = Q_g K^T
-            const uint32_t qa = sq + g * kTileBytes, ka = sk + st * kTileBytes;
+            const uint64_t qd = tc::smem_desc_sw128(sq + g * kTileBytes, 16, 1024);
+            const uint64_t kd = tc::smem_desc_sw128(sk + st * kTileBytes, 16, 1024);
+            const uint32_t dt = tbase + kTileRows * g;
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
                 const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-                tc::mma_ss(tbase + kTileRows * g, tc::smem_desc_sw128(qa + off, 16, 1024),
-                           tc::smem_desc_sw128(ka + off, 16, 1024), id_qk, kk > 0);
+                tc::mma_ss(dt, desc_off(qd, off), desc_off(kd, off), id_qk, kk > 0);
             }
         };
         auto issue_pv = [&](int g, int st, bool acc) {  // O_g += P_g V
-            const uint32_t va = sv + st * kTileBytes;
+            const uint64_t vd = tc::smem_desc_sw128(sv + st * kTileBytes, kHalfBytes, 1024);
+            const uint32_t dt = tbase + 256 + kTileRows * g, at = tbase + kTileRows * g;
 #pragma unroll
             for (int kk = 0; kk < kTileRows / 16; ++kk)
-                tc::mma_ts(tbase + 256 + kTileRows * g, tbase + kTileRows * g + kk * 8,
-                           tc::smem_desc_sw128(va + kk * 2048, kHalfBytes, 1024), id_pv, (acc || kk > 0) ? 1u : 0u);
+                tc::mma_ts(dt, at + kk * 8, desc_off(vd, kk * 2048), id_pv, (acc || kk > 0) ? 1u : 0u);
         };
         int tctr = 0;
         int nq[2] = {0, 0}, np_[2] = {0, 0};
@@ -644,6 +667,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) {
                         issue_s(g, st);
                         tc::commit(s_full + g);
+                        // the last MMA that reads Q_g: the producer may load the next
+                        // item's Q_g once it completes
+                        if (nt_g[g] == 1) tc::commit(q_empty + g);
                     }
                     __syncwarp();
                 }
@@ -652,8 +678,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
             }
             for (int j = 0; j < nt && ok; ++j) {
-                const int t = tctr + j, st = t & 1;
-                if (!wait_bar_warp(v_full + st, (t >> 1) & 1, abort_flag)) {
+                const int t = tctr + j, vs = t % kVStages;
+                if (!wait_bar_warp(v_full + vs, (t / kVStages) & 1, abort_flag)) {
                     fail(FCCI_DEV_ERR_TIMEOUT);
                     ok = false;
                     break;
@@ -661,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (j == nt - 1 && kTileRows * (j + 1) > keys) {
                     // keys past the end of the sequence: zero their V rows (arena
                     // rows beyond T_b + n_b may hold anything, and 0 * NaN = NaN)
-                    uint8_t* vt = sm + Smem::kV + st * kTileBytes;
+                    uint8_t* vt = sm + Smem::kV + vs * kTileBytes;
                     const int r0 = keys - kTileRows * j;
                     for (int c = r0 * 16 + lane; c < kTileRows * 16; c += 32) {
                         const int r = c >> 4, half = (c >> 3) & 1, ch = c & 7;
@@ -681,7 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     ++np_[g];
                     tc::fence_after_sync();
-                    if (lane == 0) issue_pv(g, st, j > 0);
+                    if (lane == 0) issue_pv(g, vs, j > 0);
                     __syncwarp();
                     if (j + 1 < nt_g[g]) {
                         if (!next_k) {
@@ -696,17 +722,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (lane == 0) {
                             issue_s(g, (t + 1) & 1);
                             tc::commit(s_full + g);
+                            if (j + 2 == nt_g[g]) tc::commit(q_empty + g);  // last S_g of the item
                         }
                     } else if (lane == 0) {
                         tc::commit(o_full + g);
-                        tc::commit(q_empty + g);
                     }
                     __syncwarp();
                 }
                 if (!ok) break;
                 if (lane == 0) {
                     if (next_k) tc::commit(k_empty + ((t + 1) & 1));
-                    tc::commit(v_empty + st);
+                    tc::commit(v_empty + vs);
                 }
                 __syncwarp();
             }
