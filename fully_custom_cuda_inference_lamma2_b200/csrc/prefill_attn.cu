@@ -24,7 +24,7 @@
 //
 // Inside a CTA (384 threads):
 //   warp 0      TMA producer: Q0/Q1 tiles, then K_j / V_j tiles (128 keys each)
-//               through a two-stage ring per operand
+//               through a two-stage (K) and a three-stage (V) ring
 //   warp 1      TMEM owner and MMA issuer (one thread issues, the warp zeroes the
 //               V rows past the end of a sequence before they are multiplied)
 //   warps 4-7   softmax of Q0 rows, warps 8-11 softmax of Q1 rows: thread r owns
@@ -1012,6 +1012,7 @@ static int setup(const fcci_prefill_desc* d, Launch& x) {
     if (x.dev < 0 || x.dev >= 128) return set_status(FCCI_EINVAL, "fcci_prefill_attention: device index");
     static std::once_flag flags[128];
     static cudaError_t attr_err[128];
+    static bool regs_short[128];
     const int dev = x.dev;
     std::call_once(flags[dev], [dev]() {
         attr_err[dev] =
@@ -1019,8 +1020,23 @@ static int setup(const fcci_prefill_desc* d, Launch& x) {
         if (attr_err[dev] == cudaSuccess)
             attr_err[dev] =
                 cudaFuncSetAttribute(prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+#if FCCI_PF_REG_SPLIT
+        // The softmax warpgroups' setmaxnreg.inc takes registers from the block's
+        // launch allocation: if the kernel were built with fewer registers per
+        // thread than the split assumes, the increase would wait forever. Refuse
+        // to launch such a build.
+        if (attr_err[dev] == cudaSuccess) {
+            cudaFuncAttributes fa;
+            attr_err[dev] = cudaFuncGetAttributes(&fa, prefill_attn_kernel);
+            regs_short[dev] =
+                attr_err[dev] == cudaSuccess && fa.numRegs * kThreads < 128 * kRegsLow + 256 * kRegsHigh;
+        }
+#endif
     });
     if (attr_err[dev] != cudaSuccess) return set_cuda_status(attr_err[dev]);
+    if (regs_short[dev])
+        return set_status(FCCI_EUNSUPPORTED,
+                          "fcci_prefill_attention: kernel built with fewer registers than its warpgroup split needs");
     return FCCI_OK;
 }
 
